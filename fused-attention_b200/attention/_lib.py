@@ -1,0 +1,176 @@
+"""ctypes binding of libfa_sm100.so, the sm_100a kernels behind a C ABI (include/fa_sm100.h).
+
+This module is self-contained (it imports nothing else from the package) so the public kernel
+files can load it by path when they are themselves imported by path, the way the reference's
+runners import a kernel file (`tests/fused/run_correctness.py:107-122` in the reference).
+
+There is no fallback: if the shared library is missing or the device is not an sm_100 GPU, the
+calls raise.  Tensors cross the boundary as raw device pointers plus sizes; the CUDA stream is
+torch's current stream, so the kernels order with surrounding torch work exactly like the
+reference's `ct.launch(torch.cuda.current_stream(), ...)` (attention/fused/fused.py:75).
+"""
+import ctypes
+import os
+import threading
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libfa_sm100.so")
+ABI_VERSION = 1
+
+FA_OK = 0
+FA_ERR_INVALID_ARG = 1
+FA_ERR_UNSUPPORTED = 2
+FA_ERR_ALIGNMENT = 3
+FA_ERR_CUDA = 4
+FA_ERR_DRIVER = 5
+FA_ERR_DEVICE = 6
+
+# exported symbol -> (argtypes) ; every entry point returns int
+_VP, _I, _FP = ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p
+SIGNATURES = {
+    "fa_abi_version": [],
+    "fa_strerror": [_I],
+    "fa_last_cuda_error": [],
+    "fa_fwd": [_VP, _VP, _VP, _VP, _FP, _I, _I, _I, _I, _I, _I, _I, _I, _VP, _VP],
+    "fa_bwd_preprocess": [_VP, _VP, _FP, _I, _I, _I, _I, _I, _VP, _VP],
+    "fa_bwd_dkdv": [_VP, _VP, _VP, _VP, _FP, _FP, _VP, _VP, _I, _I, _I, _I, _I, _I, _I, _I, _VP, _VP],
+    "fa_bwd_dq": [_VP, _VP, _VP, _VP, _FP, _FP, _VP, _I, _I, _I, _I, _I, _I, _I, _I, _VP, _VP],
+}
+_RESTYPES = {"fa_strerror": ctypes.c_char_p, "fa_last_cuda_error": ctypes.c_char_p}
+
+_lib = None
+_lock = threading.Lock()
+_status = {}  # device index -> int32[4] status tensor
+
+DTYPE_CODES = {torch.float16: 0, torch.bfloat16: 1}
+
+
+class KernelError(RuntimeError):
+    """A device-side pipeline wait timed out (the kernel stopped instead of hanging)."""
+
+
+def load():
+    """Load (once) and return the ctypes handle of libfa_sm100.so."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"{LIB_PATH} is not built; run `python fused-attention_b200/build.py` "
+                    "(this library has no non-CUDA fallback)")
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, args in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = args
+                fn.restype = _RESTYPES.get(name, ctypes.c_int)
+            if lib.fa_abi_version() != ABI_VERSION:
+                raise RuntimeError(f"libfa_sm100.so ABI {lib.fa_abi_version()} != {ABI_VERSION}; rebuild it")
+            _lib = lib
+    return _lib
+
+
+def status_tensor(device):
+    """Per-device int32[4] status word the kernels report pipeline timeouts into."""
+    idx = torch.device(device).index
+    if idx is None:
+        idx = torch.cuda.current_device()
+    st = _status.get(idx)
+    if st is None:
+        st = torch.zeros(4, dtype=torch.int32, device=f"cuda:{idx}")
+        _status[idx] = st
+    return st
+
+
+def check_status(device=None, reset=True):
+    """Synchronise `device` and raise KernelError if a kernel recorded a timeout."""
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    st = status_tensor(device)
+    vals = st.tolist()  # synchronises with the device
+    if vals[0] != 0:
+        if reset:
+            st.zero_()
+        raise KernelError(f"device pipeline error code {vals[0]} (cta {vals[1]}, thread {vals[2]})")
+
+
+def _raise(rc, what):
+    lib = load()
+    msg = lib.fa_strerror(rc).decode()
+    if rc == FA_ERR_CUDA:
+        msg += ": " + lib.fa_last_cuda_error().decode()
+    if rc in (FA_ERR_INVALID_ARG,):
+        raise ValueError(f"{what}: {msg}")
+    if rc in (FA_ERR_UNSUPPORTED, FA_ERR_ALIGNMENT):
+        raise ValueError(f"{what}: {msg}")
+    raise RuntimeError(f"{what}: {msg}")
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _dtype_code(t):
+    code = DTYPE_CODES.get(t.dtype)
+    if code is None:
+        raise TypeError(f"dtype {t.dtype} is not supported (float16 or bfloat16)")
+    return code
+
+
+def fwd(q, k, v, o, lse, tile_m, tile_n):
+    """Enqueue the forward kernel: o (and lse if not None) from q, k, v (all contiguous CUDA)."""
+    lib = load()
+    B, H, S, D = q.shape
+    H_kv = k.shape[1]
+    with torch.cuda.device(q.device):
+        rc = lib.fa_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), B, H, H_kv, S, D,
+                        _dtype_code(q), int(tile_m), int(tile_n),
+                        _ptr(status_tensor(q.device)), _stream(q))
+    if rc != FA_OK:
+        _raise(rc, "fa_fwd")
+
+
+def bwd_preprocess(o, do, delta):
+    lib = load()
+    B, H, S, D = o.shape
+    with torch.cuda.device(o.device):
+        rc = lib.fa_bwd_preprocess(_ptr(o), _ptr(do), _ptr(delta), B, H, S, D, _dtype_code(o),
+                                   _ptr(status_tensor(o.device)), _stream(o))
+    if rc != FA_OK:
+        _raise(rc, "fa_bwd_preprocess")
+
+
+def bwd_dkdv(q, k, v, do, lse, delta, dk, dv, tile_m, tile_n):
+    lib = load()
+    B, H, S, D = q.shape
+    H_kv = k.shape[1]
+    with torch.cuda.device(q.device):
+        rc = lib.fa_bwd_dkdv(_ptr(q), _ptr(k), _ptr(v), _ptr(do), _ptr(lse), _ptr(delta),
+                             _ptr(dk), _ptr(dv), B, H, H_kv, S, D, _dtype_code(q),
+                             int(tile_m), int(tile_n), _ptr(status_tensor(q.device)), _stream(q))
+    if rc != FA_OK:
+        _raise(rc, "fa_bwd_dkdv")
+
+
+def bwd_dq(q, k, v, do, lse, delta, dq, tile_m, tile_n):
+    lib = load()
+    B, H, S, D = q.shape
+    H_kv = k.shape[1]
+    with torch.cuda.device(q.device):
+        rc = lib.fa_bwd_dq(_ptr(q), _ptr(k), _ptr(v), _ptr(do), _ptr(lse), _ptr(delta), _ptr(dq),
+                           B, H, H_kv, S, D, _dtype_code(q), int(tile_m), int(tile_n),
+                           _ptr(status_tensor(q.device)), _stream(q))
+    if rc != FA_OK:
+        _raise(rc, "fa_bwd_dq")
+
+
+def load_by_path():
+    """Return this module (used by files that are imported by path)."""
+    import sys
+    return sys.modules[__name__]

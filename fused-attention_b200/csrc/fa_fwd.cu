@@ -1,0 +1,429 @@
+// Causal attention forward for sm_100a (B200): TMA + tcgen05 UMMA + TMEM, warp-specialised.
+//
+// Computes, per (batch, query head), O = softmax(Q K^T / sqrt(D) + causal mask) V and,
+// optionally, the log2-domain row statistic LSE = m + log2(l) of the scaled scores
+// (the quantity the reference's LSE-saving forward stores:
+// attention/backward/fused_backward.py:60-62,169).  Online softmax in exp2 with the
+// folded constant log2(e)/sqrt(D) follows attention/fused/fused.py:34-64; GQA (query head h
+// reads K/V head h // (H / H_kv)) follows attention/gqa/fused_gqa.py:18,37-39.
+//
+// CTA work unit: two 128-row query tiles that read the SAME K/V head:
+//   mode 0: q-tiles (2c, 2c+1) of one head          (MHA, odd GQA groups)
+//   mode 1: q-tile i of query heads (2p, 2p+1)      (even GQA groups: K/V tile shared)
+// Warp roles (384 threads, warpgroup aligned):
+//   warps 0-3   softmax for tile 0 (one TMEM lane = one query row per thread)
+//   warps 4-7   softmax for tile 1
+//   warp 8      TMA producer: Q tiles once, then a K/V shared-memory ring
+//   warp 9      UMMA issuer: S_t = Q_t K_j^T into TMEM, O_t += P_t V_j with P_t read from TMEM
+//   warps 10-11 idle
+// TMEM (512 columns): S_0 | S_1 | O_0 | O_1, 128 columns each; P_t (16-bit) overwrites the first
+// half of S_t once the row has been read into registers.  The two softmax warpgroups ping-pong:
+// while one converts its S tile the tensor core runs the other tile's P V and next Q K^T.
+// O is rescaled in TMEM only when a row max grows by more than 2^8 (otherwise the stale max is
+// kept, which is exact because numerator and denominator use the same offset).
+#include "fa_internal.h"
+#include "fa_sm100.cuh"
+
+namespace fa {
+namespace {
+
+constexpr int kThreads = 384;
+constexpr int kWarpProducer = 8;
+constexpr int kWarpMma = 9;
+constexpr int kBM = 128;
+constexpr uint32_t kTmemCols = 512;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only if the max grows > 256x
+
+template <int D, int BN>
+struct FwdCfg {
+  static constexpr int kChunks = D / 64;            // 64-column (128-byte) swizzle chunks
+  static constexpr int kQChunkBytes = kBM * 128;
+  static constexpr int kKVChunkBytes = BN * 128;
+  static constexpr int kQBytes = kBM * D * 2;
+  static constexpr int kKVBytes = BN * D * 2;
+  static constexpr int kStageBytes = 2 * kKVBytes;  // K tile + V tile
+  static constexpr int kBudget = 225 * 1024;
+  static constexpr int kStagesFit = (kBudget - 2 * kQBytes - 1024) / kStageBytes;
+  static constexpr int kStages = kStagesFit > 4 ? 4 : kStagesFit;
+  static_assert(kStages >= 2, "need at least a double-buffered K/V ring");
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffKV = 2 * kQBytes;
+  static constexpr int kOffBar = kOffKV + kStages * kStageBytes;
+  static constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers + 1 KiB alignment slack
+};
+
+// barrier slots
+enum : int {
+  BAR_Q = 0,
+  BAR_KFULL = 1,    // + stage (4)
+  BAR_VFULL = 5,    // + stage (4)
+  BAR_KVEMPTY = 9,  // + stage (4)
+  BAR_SFULL = 13,   // + tile (2)
+  BAR_PFULL = 15,   // + tile (2)
+  BAR_OFULL = 17,   // + tile (2)
+  BAR_DRAIN = 19,
+  BAR_COUNT = 20
+};
+
+struct QTile {
+  int bh;  // b * H + h (query head)
+  int qt;  // 128-row query tile index
+};
+
+struct Work {
+  QTile t[2];
+  int ntiles;  // 1 or 2
+  int bh_kv;   // b * H_kv + kv head
+  int nkv[2];  // K/V tiles visible to each query tile
+};
+
+template <int BN>
+__device__ __forceinline__ int kv_tiles_for(int qt, int S) {
+  int last_row = min(qt * kBM + kBM - 1, S - 1);
+  return last_row / BN + 1;
+}
+
+template <int BN>
+__device__ __forceinline__ Work decode_work(const FwdParams& p, int item) {
+  Work w;
+  if (p.mode == 0) {
+    const int ncp = (p.nq + 1) / 2;
+    const int bh = item / ncp;
+    const int c = ncp - 1 - (item - bh * ncp);  // heavy (late) tile pairs of a head first
+    w.t[0] = {bh, 2 * c};
+    w.t[1] = {bh, 2 * c + 1};
+    w.ntiles = (2 * c + 1 < p.nq) ? 2 : 1;
+    const int b = bh / p.H, h = bh - b * p.H;
+    w.bh_kv = b * p.H_kv + h / p.group;
+  } else {
+    const int pairs_per_b = p.H / 2;
+    const int pi = item / p.nq;
+    const int i = p.nq - 1 - (item - pi * p.nq);
+    const int b = pi / pairs_per_b, hp = pi - b * pairs_per_b;
+    const int h = 2 * hp;
+    w.t[0] = {b * p.H + h, i};
+    w.t[1] = {b * p.H + h + 1, i};
+    w.ntiles = 2;
+    w.bh_kv = b * p.H_kv + h / p.group;
+  }
+  w.nkv[0] = kv_tiles_for<BN>(w.t[0].qt, p.S);
+  w.nkv[1] = (w.ntiles == 2) ? kv_tiles_for<BN>(w.t[1].qt, p.S) : 0;
+  return w;
+}
+
+// Bounded wait used only while tearing down: ignores the abort flag so that copies and MMAs
+// already in flight are always waited for (they complete on their own).
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int* status) {
+  if (mbar_try_wait(bar, parity)) return;
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > FA_WAIT_TIMEOUT_NS) {
+      record_error(status, kDevTimeoutDrain, static_cast<int>(threadIdx.x));
+      return;
+    }
+  }
+}
+
+template <int D, int BN, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
+  using C = FwdCfg<D, BN>;
+  constexpr int ST = C::kStages;
+  constexpr uint32_t IDESC_S = idesc_f16(BF16, kBM, BN, false, false);  // Q, K both K-major
+  constexpr uint32_t IDESC_O = idesc_f16(BF16, kBM, D, false, true);    // P (TMEM), V MN-major
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + C::kOffBar + 8 * BAR_COUNT);
+  volatile int* abort_slot = reinterpret_cast<volatile int*>(smem + C::kOffBar + 8 * BAR_COUNT + 4);
+  auto bar = [&](int i) -> uint32_t { return smem_u32(bars + i); };
+  const uint32_t sQ = base + C::kOffQ;
+  const uint32_t sKV = base + C::kOffKV;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  // A failed CTA leaves a non-zero status word: every later CTA stops before touching TMEM.
+  if (threadIdx.x == 0) *abort_slot = ld_status(p.status);
+  __syncthreads();
+  if (*abort_slot != 0) return;
+
+  const Work w = decode_work<BN>(p, blockIdx.x);
+  const int nmax = max(w.nkv[0], w.nkv[1]);
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    mbar_init(bar(BAR_Q), 1);
+    for (int s = 0; s < 4; ++s) {
+      mbar_init(bar(BAR_KFULL + s), 1);
+      mbar_init(bar(BAR_VFULL + s), 1);
+      mbar_init(bar(BAR_KVEMPTY + s), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(BAR_SFULL + t), 1);
+      mbar_init(bar(BAR_PFULL + t), 128);
+      mbar_init(bar(BAR_OFULL + t), 1);
+    }
+    mbar_init(bar(BAR_DRAIN), 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(const_cast<uint32_t*>(tmem_slot)), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kWarpProducer) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_q = policy_evict_first();
+      const uint64_t pol_kv = policy_evict_last();
+      mbar_arrive_expect_tx(bar(BAR_Q), w.ntiles * C::kQBytes);
+      for (int t = 0; t < w.ntiles; ++t)
+        for (int c = 0; c < C::kChunks; ++c)
+          tma_load_3d(sQ + t * C::kQBytes + c * C::kQChunkBytes, &tmQ, bar(BAR_Q), c * 64,
+                      w.t[t].qt * kBM, w.t[t].bh, pol_q);
+      int issued = 0;
+      for (int j = 0; j < nmax; ++j) {
+        const int s = j % ST;
+        const uint32_t ph = (j / ST) & 1;
+        if (!mbar_wait(bar(BAR_KVEMPTY + s), ph ^ 1, p.status, kDevTimeoutKVEmpty)) break;
+        const uint32_t sK = sKV + s * C::kStageBytes;
+        const uint32_t sV = sK + C::kKVBytes;
+        mbar_arrive_expect_tx(bar(BAR_KFULL + s), C::kKVBytes);
+        for (int c = 0; c < C::kChunks; ++c)
+          tma_load_3d(sK + c * C::kKVChunkBytes, &tmK, bar(BAR_KFULL + s), c * 64, j * BN,
+                      w.bh_kv, pol_kv);
+        mbar_arrive_expect_tx(bar(BAR_VFULL + s), C::kKVBytes);
+        for (int c = 0; c < C::kChunks; ++c)
+          tma_load_3d(sV + c * C::kKVChunkBytes, &tmV, bar(BAR_VFULL + s), c * 64, j * BN,
+                      w.bh_kv, pol_kv);
+        ++issued;
+      }
+      // Never leave the CTA with a copy still writing into shared memory.
+      drain_wait(bar(BAR_Q), 0, p.status);
+      for (int j = max(0, issued - ST); j < issued; ++j) {
+        drain_wait(bar(BAR_KFULL + j % ST), (j / ST) & 1, p.status);
+        drain_wait(bar(BAR_VFULL + j % ST), (j / ST) & 1, p.status);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kWarpMma) {
+    // ------------------------------------------------------------ UMMA issuer
+    if (lane == 0) {
+      auto issue_s = [&](int t, int s) {
+        const uint32_t qa = sQ + t * C::kQBytes;
+        const uint32_t kb = sKV + s * C::kStageBytes;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k % 4) * 32;  // 16 elements = 32 B inside the 128-B row
+          const uint64_t ad = sdesc_sw128(qa + (k / 4) * C::kQChunkBytes + off, 16, 1024);
+          const uint64_t bd = sdesc_sw128(kb + (k / 4) * C::kKVChunkBytes + off, 16, 1024);
+          umma_ss(tmem + t * 128, ad, bd, IDESC_S, k > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int t, int s, bool acc) {
+        const uint32_t vb = sKV + s * C::kStageBytes + C::kKVBytes;
+#pragma unroll
+        for (int k = 0; k < BN / 16; ++k) {
+          const uint64_t bd = sdesc_sw128(vb + k * 2048, C::kKVChunkBytes, 1024);
+          umma_ts(tmem + 256 + t * 128, tmem + t * 128 + k * 8, bd, IDESC_O,
+                  (acc || k > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(bar(BAR_Q), 0, p.status, kDevTimeoutQ) &&
+                mbar_wait(bar(BAR_KFULL + 0), 0, p.status, kDevTimeoutKV);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < w.ntiles; ++t) {
+          issue_s(t, 0);
+          umma_commit(bar(BAR_SFULL + t));
+        }
+      }
+      for (int j = 0; ok && j < nmax; ++j) {
+        const int s = j % ST;
+        ok = mbar_wait(bar(BAR_VFULL + s), (j / ST) & 1, p.status, kDevTimeoutKV);
+        if (!ok) break;
+        tc_fence_after();
+        bool next_k_ready = false;
+        const int s1 = (j + 1) % ST;
+        for (int t = 0; t < w.ntiles && ok; ++t) {
+          if (j >= w.nkv[t]) continue;
+          ok = mbar_wait(bar(BAR_PFULL + t), j & 1, p.status, kDevTimeoutP);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(t, s, j > 0);
+          if (j + 1 == w.nkv[t]) {
+            umma_commit(bar(BAR_OFULL + t));
+          } else {
+            if (!next_k_ready) {
+              ok = mbar_wait(bar(BAR_KFULL + s1), ((j + 1) / ST) & 1, p.status, kDevTimeoutKV);
+              if (!ok) break;
+              tc_fence_after();
+              next_k_ready = true;
+            }
+            issue_s(t, s1);
+            umma_commit(bar(BAR_SFULL + t));
+          }
+        }
+        umma_commit(bar(BAR_KVEMPTY + s));
+      }
+      // All MMAs issued by this thread must finish before TMEM is released.
+      umma_commit(bar(BAR_DRAIN));
+      drain_wait(bar(BAR_DRAIN), 0, p.status);
+    }
+    __syncwarp();
+  } else if (warp < 8) {
+    // ------------------------------------------------------------ softmax / epilogue
+    const int t = warp / 4;
+    if (t < w.ntiles) {
+      const QTile tile = w.t[t];
+      const int nkv = w.nkv[t];
+      const int wq = warp % 4;  // TMEM lane quarter this warp may access
+      const int row = wq * 32 + lane;
+      const int qrow = tile.qt * kBM + row;
+      const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+      const uint32_t tS = tmem + t * 128 + lane_off;
+      const uint32_t tO = tmem + 256 + t * 128 + lane_off;
+      const float scale = p.scale_log2;
+      float m_used = -INFINITY;
+      float l = 0.f;
+      bool ok = true;
+      for (int j = 0; j < nkv; ++j) {
+        ok = mbar_wait(bar(BAR_SFULL + t), j & 1, p.status, kDevTimeoutS);
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t r[BN / 32][32];
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + c * 32, r[c]);
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) tmem_ld_wait(r[c]);
+        const int kbase = j * BN;
+        if (kbase + BN - 1 > tile.qt * kBM || kbase + BN > p.S) {
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int key = kbase + c * 32 + i;
+              if (key > qrow || key >= p.S) r[c][i] = __float_as_uint(-INFINITY);
+            }
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(r[c][i]));
+        const float mt = mx * scale;
+        const bool upd = mt > m_used + kRescaleThreshold;
+        const float m_new = upd ? mt : m_used;
+        const float alpha = ex2_approx(m_used - m_new);
+        const float neg_m = -m_new;
+        float sum = 0.f;
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = ex2_approx(fmaf(__uint_as_float(r[c][2 * i]), scale, neg_m));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(r[c][2 * i + 1]), scale, neg_m));
+            sum += p0 + p1;
+            pk[i] = pack2<BF16>(p0, p1);
+          }
+          tmem_st16(tS + c * 16, pk);
+        }
+        l = l * alpha + sum;
+        m_used = m_new;
+        // Rescale the running O of this warp's rows if any row's max moved (P V of tile j-1 is
+        // complete: it was issued before S_t(j), whose completion we waited for).
+        if (j > 0 && __any_sync(0xffffffffu, upd)) {
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_ld_wait(o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(tO + c * 32, o);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar(BAR_PFULL + t));
+      }
+      if (ok) ok = mbar_wait(bar(BAR_OFULL + t), 0, p.status, kDevTimeoutO);
+      if (ok) {
+        tc_fence_after();
+        const float inv_l = 1.0f / l;
+        uint8_t* orow = reinterpret_cast<uint8_t*>(p.o) +
+                        (static_cast<size_t>(tile.bh) * p.S + qrow) * (D * 2);
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_ld_wait(o);
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pk[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l,
+                                __uint_as_float(o[2 * i + 1]) * inv_l);
+          if (qrow < p.S) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          }
+        }
+        if (p.lse != nullptr && qrow < p.S)
+          p.lse[static_cast<size_t>(tile.bh) * p.S + qrow] = m_used + log2f(l);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <int D, int BN, bool BF16>
+cudaError_t launch_fwd_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                         const FwdParams& p, cudaStream_t stream) {
+  using C = FwdCfg<D, BN>;
+  auto kern = fa_fwd_kernel<D, BN, BF16>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  kern<<<p.n_items, kThreads, C::kSmemBytes, stream>>>(tmQ, tmK, tmV, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_fwd(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                       const FwdParams& p, int D, int block_n, bool bf16, cudaStream_t stream) {
+#define FA_FWD_CASE(DD, NN, BB)                                              \
+  if (D == DD && block_n == NN && bf16 == BB)                                \
+    return launch_fwd_t<DD, NN, BB>(tmQ, tmK, tmV, p, stream);
+  FA_FWD_CASE(64, 64, false)
+  FA_FWD_CASE(64, 128, false)
+  FA_FWD_CASE(128, 64, false)
+  FA_FWD_CASE(128, 128, false)
+  FA_FWD_CASE(64, 64, true)
+  FA_FWD_CASE(64, 128, true)
+  FA_FWD_CASE(128, 64, true)
+  FA_FWD_CASE(128, 128, true)
+#undef FA_FWD_CASE
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace fa

@@ -1,0 +1,58 @@
+// Host-side declarations shared by the C-ABI layer (fa_api.cu) and the kernel files.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace fa {
+
+// Parameters of one forward launch (plain values; tensor maps travel separately as
+// __grid_constant__ kernel parameters).
+struct FwdParams {
+  void* o;            // [B, H, S, D] output, same dtype as q
+  float* lse;         // [B, H, S] log2-domain LSE, or nullptr
+  int* status;        // int32[4] device status word (see DeviceError)
+  int S;              // sequence length (queries == keys)
+  int H;              // query heads
+  int H_kv;           // key/value heads
+  int group;          // H / H_kv
+  int B;              // batch
+  int nq;             // number of 128-row query tiles = ceil(S / 128)
+  int mode;           // 0: a CTA takes q-tiles (2c, 2c+1) of one head; 1: q-tile i of heads (2p, 2p+1)
+  int n_items;        // grid size
+  float scale_log2;   // log2(e) / sqrt(D)
+};
+
+struct BwdParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* o;
+  const void* dO;
+  const float* lse;   // [B, H, S] log2 domain
+  float* delta;       // [B, H, S] rowsum(dO * O) (written by the preprocess kernel)
+  void* dq;
+  void* dk;
+  void* dv;
+  int* status;
+  int S, H, H_kv, group, B, D;
+  int nq;             // ceil(S / 128)
+  int n_items;
+  float scale_log2;   // log2(e) / sqrt(D)
+  float sm_scale;     // 1 / sqrt(D)
+};
+
+// Launchers implemented in the kernel translation units.  They return a cudaError_t.
+cudaError_t launch_fwd(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                       const FwdParams& p, int D, int block_n, bool bf16, cudaStream_t stream);
+
+cudaError_t launch_bwd_preprocess(const BwdParams& p, bool bf16, cudaStream_t stream);
+cudaError_t launch_bwd_dkdv(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                            const CUtensorMap& tmdO, const BwdParams& p, bool bf16,
+                            cudaStream_t stream);
+cudaError_t launch_bwd_dq(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                          const CUtensorMap& tmdO, const BwdParams& p, bool bf16,
+                          cudaStream_t stream);
+
+}  // namespace fa

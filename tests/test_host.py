@@ -1,0 +1,132 @@
+"""Host-side logic that runs without a GPU: the C-ABI library loads and exports every declared
+symbol, argument validation in C and Python, the input contracts and the CLI exit codes."""
+import ctypes
+import os
+import re
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(REPO, "fused-attention_b200")
+HEADER = os.path.join(REPO, "include", "fa_sm100.h")
+
+
+def _native():
+    from attention.fused.fused import _native as n
+    return n()
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"FA_API\s+[\w\s\*]*?\b(fa_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_abi():
+    syms = declared_symbols()
+    assert {"fa_fwd", "fa_bwd_preprocess", "fa_bwd_dkdv", "fa_bwd_dq", "fa_strerror",
+            "fa_abi_version", "fa_last_cuda_error"} <= set(syms)
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = ctypes.CDLL(_native().LIB_PATH)
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert set(_native().SIGNATURES) >= set(declared_symbols())
+    assert _native().load().fa_abi_version() == _native().ABI_VERSION
+
+
+def test_strerror_covers_codes():
+    lib = _native().load()
+    for code in range(0, 7):
+        assert lib.fa_strerror(code).decode() not in ("", "unknown error code")
+    assert lib.fa_strerror(99).decode() == "unknown error code"
+
+
+def _fwd_rc(**kw):
+    lib = _native().load()
+    args = dict(q=8, k=8, v=8, o=8, lse=None, B=1, H=8, H_kv=8, S=128, D=64, dtype=0, tm=64, tn=64,
+                st=16)
+    args.update(kw)
+    vp = ctypes.c_void_p
+    return lib.fa_fwd(vp(args["q"]), vp(args["k"]), vp(args["v"]), vp(args["o"]), args["lse"],
+                      args["B"], args["H"], args["H_kv"], args["S"], args["D"], args["dtype"],
+                      args["tm"], args["tn"], vp(args["st"]), None)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(B=0), 1), (dict(S=0), 1), (dict(H=6, H_kv=4), 1), (dict(q=0), 1), (dict(st=0), 1),
+    (dict(D=32), 2), (dict(D=96), 2), (dict(dtype=2), 2), (dict(tm=32), 2), (dict(tn=256), 2),
+])
+def test_c_abi_rejects_bad_arguments_before_touching_the_device(kw, code):
+    assert _fwd_rc(**kw) == code
+
+
+def test_python_wrappers_keep_reference_errors():
+    from attention.fused.fused import fused_attention
+    from attention.gqa.fused_gqa import fused_gqa_attention
+    from attention.backward.fused_backward import fused_attention_autograd
+    q = torch.zeros(1, 2, 96, 64, dtype=torch.float16)
+    with pytest.raises(ValueError, match="divisible"):
+        fused_attention(q, q, q, 64, 64)
+    k = torch.zeros(1, 3, 128, 64, dtype=torch.float16)
+    q2 = torch.zeros(1, 4, 128, 64, dtype=torch.float16)
+    with pytest.raises(ValueError, match="GQA needs"):
+        fused_gqa_attention(q2, k, k)
+    with pytest.raises(TypeError):
+        fused_attention_autograd(q2.float(), q2.float(), q2.float())
+    with pytest.raises(ValueError):
+        fused_attention_autograd(q2, k, k)
+
+
+def test_validation_contract():
+    from attention.fused.validation import ValidationError, validate_qkv
+    from attention.gqa.validation_gqa import validate_qkv as validate_gqa
+    ok = np.zeros((2, 4, 128, 64), np.float16)
+    validate_qkv(ok, ok, ok, 64, 64)
+    with pytest.raises(ValidationError, match="only float16 and bfloat16"):
+        validate_qkv(ok.astype(np.float32), ok, ok, 64, 64)
+    with pytest.raises(ValidationError, match="head dim D=32"):
+        z = np.zeros((1, 1, 128, 32), np.float16)
+        validate_qkv(z, z, z, 64, 64)
+    with pytest.raises(ValidationError, match="not divisible"):
+        validate_qkv(ok, ok, ok, 128, 48)
+    with pytest.raises(ValidationError, match="head count mismatch"):
+        validate_qkv(ok, np.ascontiguousarray(ok[:, :2]), np.ascontiguousarray(ok[:, :2]), 64, 64)
+    kv = np.zeros((2, 2, 128, 64), np.float16)
+    assert validate_gqa(ok, kv, kv, 64, 64) == 2
+    with pytest.raises(ValidationError, match="not divisible by KV heads"):
+        kv3 = np.zeros((2, 3, 128, 64), np.float16)
+        validate_gqa(ok, kv3, kv3, 64, 64)
+    t = torch.zeros(1, 1, 128, 64, dtype=torch.bfloat16)
+    validate_qkv(t, t, t, 64, 64)
+
+
+def _cli(script, *args):
+    r = subprocess.run([sys.executable, os.path.join(PKG, script), *args], capture_output=True, text=True,
+                       env={**os.environ, "CUDA_VISIBLE_DEVICES": os.environ.get("CUDA_VISIBLE_DEVICES", "")})
+    return r.returncode, r.stderr
+
+
+def test_cli_exit_codes(tmp_path):
+    missing = tmp_path / "nope.npz"
+    rc, err = _cli("run_attention.py", "--input", str(missing), "--output", str(tmp_path / "o.npy"))
+    assert rc == 2 and "not found" in err
+    bad = tmp_path / "bad.npz"
+    np.savez(bad, Q=np.zeros((1, 1, 128, 64), np.float32), K=np.zeros((1, 1, 128, 64), np.float32),
+             V=np.zeros((1, 1, 128, 64), np.float32))
+    rc, err = _cli("run_attention.py", "--input", str(bad), "--output", str(tmp_path / "o.npy"))
+    assert rc == 2 and "dtype" in err
+    miss_v = tmp_path / "mv.npz"
+    np.savez(miss_v, Q=np.zeros((1, 1, 128, 64), np.float16), K=np.zeros((1, 1, 128, 64), np.float16))
+    rc, err = _cli("run_attention_gqa.py", "--input", str(miss_v), "--output", str(tmp_path / "o.npy"))
+    assert rc == 2 and "missing" in err
+    good = tmp_path / "good.npz"
+    z = np.zeros((1, 2, 128, 64), np.float16)
+    np.savez(good, Q=z, K=z[:, :1], V=z[:, :1])
+    rc, err = _cli("run_attention_gqa.py", "--input", str(good), "--output", str(tmp_path / "o.npy"),
+                   "--backend", "unfused")
+    assert rc == 1 and "not built" in err
