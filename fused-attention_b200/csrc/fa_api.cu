@@ -169,17 +169,19 @@ static int bwd_prepare(const void* q, const void* k, const void* v, const void* 
                        const float* lse, const float* delta, int B, int H, int H_kv, int S,
                        int D, int dtype, int tile_m, int tile_n, int* dev_status,
                        CUtensorMap* tmQ, CUtensorMap* tmK, CUtensorMap* tmV, CUtensorMap* tmdO,
-                       fa::BwdParams* p) {
+                       fa::BwdParams* p, int q_rows, int kv_rows) {
   if (!q || !k || !v || !dO || !lse || !delta) return FA_ERR_INVALID_ARG;
   int rc = check_common(B, H, H_kv, S, D, dtype, tile_m, tile_n, dev_status);
   if (rc != FA_OK) return rc;
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(dO) ||
-      (reinterpret_cast<uintptr_t>(lse) & 3u) || (reinterpret_cast<uintptr_t>(delta) & 3u))
+  // The backward streams whole 64-row tiles (and their lse / delta slices).
+  if (S % 64 != 0) return FA_ERR_UNSUPPORTED;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(dO) || !aligned16(lse) ||
+      !aligned16(delta))
     return FA_ERR_ALIGNMENT;
-  if ((rc = make_map(tmQ, q, B * H, S, D, dtype, 128)) != FA_OK) return rc;
-  if ((rc = make_map(tmK, k, B * H_kv, S, D, dtype, 128)) != FA_OK) return rc;
-  if ((rc = make_map(tmV, v, B * H_kv, S, D, dtype, 128)) != FA_OK) return rc;
-  if ((rc = make_map(tmdO, dO, B * H, S, D, dtype, 128)) != FA_OK) return rc;
+  if ((rc = make_map(tmQ, q, B * H, S, D, dtype, q_rows)) != FA_OK) return rc;
+  if ((rc = make_map(tmK, k, B * H_kv, S, D, dtype, kv_rows)) != FA_OK) return rc;
+  if ((rc = make_map(tmV, v, B * H_kv, S, D, dtype, kv_rows)) != FA_OK) return rc;
+  if ((rc = make_map(tmdO, dO, B * H, S, D, dtype, q_rows)) != FA_OK) return rc;
   p->q = q;
   p->k = k;
   p->v = v;
@@ -207,7 +209,7 @@ int fa_bwd_dkdv(const void* q, const void* k, const void* v, const void* dO, con
   CUtensorMap tmQ, tmK, tmV, tmdO;
   fa::BwdParams p{};
   int rc = bwd_prepare(q, k, v, dO, lse, delta, B, H, H_kv, S, D, dtype, tile_m, tile_n,
-                       dev_status, &tmQ, &tmK, &tmV, &tmdO, &p);
+                       dev_status, &tmQ, &tmK, &tmV, &tmdO, &p, /*q_rows=*/64, /*kv_rows=*/128);
   if (rc != FA_OK) return rc;
   p.dk = dk;
   p.dv = dv;
@@ -224,7 +226,7 @@ int fa_bwd_dq(const void* q, const void* k, const void* v, const void* dO, const
   CUtensorMap tmQ, tmK, tmV, tmdO;
   fa::BwdParams p{};
   int rc = bwd_prepare(q, k, v, dO, lse, delta, B, H, H_kv, S, D, dtype, tile_m, tile_n,
-                       dev_status, &tmQ, &tmK, &tmV, &tmdO, &p);
+                       dev_status, &tmQ, &tmK, &tmV, &tmdO, &p, /*q_rows=*/128, /*kv_rows=*/64);
   if (rc != FA_OK) return rc;
   p.dq = dq;
   cudaError_t e = fa::launch_bwd_dq(tmQ, tmK, tmV, tmdO, p, dtype == FA_DTYPE_BF16,

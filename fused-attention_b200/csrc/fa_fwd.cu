@@ -111,19 +111,6 @@ __device__ __forceinline__ Work decode_work(const FwdParams& p, int item) {
   return w;
 }
 
-// Bounded wait used only while tearing down: ignores the abort flag so that copies and MMAs
-// already in flight are always waited for (they complete on their own).
-__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int* status) {
-  if (mbar_try_wait(bar, parity)) return;
-  const uint64_t t0 = global_timer_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (global_timer_ns() - t0 > FA_WAIT_TIMEOUT_NS) {
-      record_error(status, kDevTimeoutDrain, static_cast<int>(threadIdx.x));
-      return;
-    }
-  }
-}
-
 template <int D, int BN, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,

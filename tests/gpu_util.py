@@ -51,3 +51,29 @@ def elementwise_ratio(out, ref, atol=2e-2, rtol=2e-2):
     if not torch.isfinite(out).all():
         return float("inf")
     return float(((out - ref).abs() / (atol + rtol * ref.abs())).max())
+
+
+def reference_grads(q, k, v, do, b, g):
+    """fp32 autograd of causal attention for batch b, K/V head g and its whole query-head group,
+    on the device.  Returns (o, dq) for the group's query heads and (dk, dv) for head g."""
+    H, H_kv = q.shape[1], k.shape[1]
+    grp = H // H_kv
+    hs = slice(g * grp, (g + 1) * grp)
+    qf = q[b, hs].float().requires_grad_(True)
+    kf = k[b, g].float().requires_grad_(True)
+    vf = v[b, g].float().requires_grad_(True)
+    N, D = q.shape[-2], q.shape[-1]
+    s = (qf @ kf.T) / math.sqrt(D)
+    mask = torch.ones(N, N, dtype=torch.bool, device=q.device).triu(1)
+    o = torch.softmax(s.masked_fill(mask, float("-inf")), dim=-1) @ vf
+    o.backward(do[b, hs].float())
+    return o.detach(), qf.grad, kf.grad, vf.grad
+
+
+def reference_backward_inputs(B, H, N, D, sigma, seed):
+    """The reference's backward case inputs: a CUDA generator seeded N + D, q, k, v scaled by
+    sigma then dO, all cast to fp16 (tests/backward/cases_backward.py:58-62 in the reference)."""
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    q, k, v = (torch.randn(B, H, N, D, device="cuda", generator=gen) * sigma for _ in range(3))
+    do = torch.randn(B, H, N, D, device="cuda", generator=gen)
+    return [t.half() for t in (q, k, v)], do.half()
