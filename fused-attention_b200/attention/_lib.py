@@ -36,6 +36,7 @@ SIGNATURES = {
     "fa_bwd_preprocess": [_VP, _VP, _FP, _I, _I, _I, _I, _I, _VP, _VP],
     "fa_bwd_dkdv": [_VP, _VP, _VP, _VP, _FP, _FP, _VP, _VP, _I, _I, _I, _I, _I, _I, _I, _I, _VP, _VP],
     "fa_bwd_dq": [_VP, _VP, _VP, _VP, _FP, _FP, _VP, _I, _I, _I, _I, _I, _I, _I, _I, _VP, _VP],
+    "fa_bwd_noalloc": [_VP, _VP, _VP, _VP, _VP, _FP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I, _I, _I, _VP, _VP],
 }
 _RESTYPES = {"fa_strerror": ctypes.c_char_p, "fa_last_cuda_error": ctypes.c_char_p}
 

@@ -18,7 +18,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 OUT = os.path.join(HERE, "attention", "libfa_sm100.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
-SOURCES = ["fa_api.cu", "fa_fwd.cu", "fa_bwd.cu"]
+SOURCES = ["fa_api.cu", "fa_fwd.cu", "fa_bwd.cu", "fa_noalloc.cu"]
 HEADERS = ["fa_sm100.cuh", "fa_internal.h"]
 
 NVCC = os.environ.get("NVCC", "nvcc")

@@ -101,6 +101,7 @@ const char* fa_strerror(int code) {
     case FA_ERR_CUDA: return "CUDA runtime error (see fa_last_cuda_error)";
     case FA_ERR_DRIVER: return "cuTensorMapEncodeTiled unavailable or rejected the tensor";
     case FA_ERR_DEVICE: return "current device is not an sm_100 (B200) GPU";
+    case FA_ERR_TOO_LARGE: return "B*H*S exceeds the static scratch of fa_bwd_noalloc (FA_NOALLOC_MAX_ROWS rows)";
     default: return "unknown error code";
   }
 }

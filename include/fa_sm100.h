@@ -43,8 +43,12 @@ enum fa_status_code {
   FA_ERR_ALIGNMENT = 3,    /* a tensor base address is not 16-byte aligned            */
   FA_ERR_CUDA = 4,         /* a CUDA runtime call failed (fa_last_cuda_error() has it) */
   FA_ERR_DRIVER = 5,       /* cuTensorMapEncodeTiled unavailable or rejected a tensor   */
-  FA_ERR_DEVICE = 6        /* current device is not compute capability 10.x (B200)      */
+  FA_ERR_DEVICE = 6,       /* current device is not compute capability 10.x (B200)      */
+  FA_ERR_TOO_LARGE = 7     /* fa_bwd_noalloc: B*H*S exceeds FA_NOALLOC_MAX_ROWS         */
 };
+
+/* Capacity of fa_bwd_noalloc's static scratch: B*H*S float32 rows (16 MiB per GPU). */
+#define FA_NOALLOC_MAX_ROWS (1 << 22)
 
 enum fa_dtype { FA_DTYPE_F16 = 0, FA_DTYPE_BF16 = 1 };
 
@@ -84,6 +88,21 @@ FA_API int fa_bwd_dq(const void* q, const void* k, const void* v, const void* dO
               const float* lse, const float* delta, void* dq,
               int B, int H, int H_kv, int S, int D, int dtype, int tile_m, int tile_n,
               int* dev_status, void* stream);
+
+/* Whole backward (delta, dk/dv, dq) for callers that cannot allocate device memory: a plugin
+ * inside a framework whose memory pool already holds nearly all of HBM, or a latency-critical
+ * path that must not call cudaMalloc (it can synchronise the device).  No counterpart in the
+ * reference.  Same tensors and rules as the three calls above, minus `delta`: the float32 delta
+ * scratch lives in a static device array of FA_NOALLOC_MAX_ROWS rows that every GPU loading the
+ * library holds until exit; larger problems (B*H*S > FA_NOALLOC_MAX_ROWS) return
+ * FA_ERR_TOO_LARGE.  This call allocates nothing (no cudaMalloc/cudaFree).  Its first call on a
+ * device resolves the array's address on that device (make it before any stream capture there).
+ * All calls on a device share the array: calls that overlap on the GPU race and must not be
+ * issued; sequential calls need no clearing (every row is rewritten before it is read). */
+FA_API int fa_bwd_noalloc(const void* q, const void* k, const void* v, const void* o,
+                          const void* dO, const float* lse, void* dq, void* dk, void* dv,
+                          int B, int H, int H_kv, int S, int D, int dtype, int tile_m, int tile_n,
+                          int* dev_status, void* stream);
 
 #ifdef __cplusplus
 }
