@@ -184,26 +184,25 @@ __device__ __forceinline__ void store_row_chunk(uint8_t* dst, const uint32_t (&v
   for (int q = 0; q < 4; ++q) d[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
 }
 
-// Issue an M=128, N=64, K=D product of two K-major SW128 tiles: outer rows x inner rows.
+// Issue an M=128, N=64, K=D product of two K-major SW128 tiles (outer rows x inner rows);
+// descriptors are precomputed bases advanced by constant offsets.
 template <int D, class C>
-__device__ __forceinline__ void umma_outer_inner(uint32_t d_tmem, uint32_t outer, uint32_t inner,
-                                                 uint32_t idesc) {
+__device__ __forceinline__ void umma_outer_inner(uint32_t d_tmem, uint64_t outer_desc,
+                                                 uint64_t inner_desc, uint32_t idesc) {
 #pragma unroll
   for (int k = 0; k < D / 16; ++k) {
-    const uint32_t off = (k % 4) * 32;
-    umma_ss(d_tmem, sdesc_sw128(outer + (k / 4) * C::kOuterChunk + off, 16, 1024),
-            sdesc_sw128(inner + (k / 4) * C::kInnerChunk + off, 16, 1024), idesc, k > 0 ? 1u : 0u);
+    umma_ss(d_tmem, desc_add(outer_desc, (k / 4) * C::kOuterChunk + (k % 4) * 32),
+            desc_add(inner_desc, (k / 4) * C::kInnerChunk + (k % 4) * 32), idesc, k > 0 ? 1u : 0u);
   }
 }
 
 // acc[128 x D] (+)= A[128 x 64] (16-bit, in TMEM) * B[64 x D] (inner tile, MN-major SW128).
 template <int D, class C>
-__device__ __forceinline__ void umma_tmem_inner(uint32_t d_tmem, uint32_t a_tmem, uint32_t inner,
-                                                uint32_t idesc, bool acc) {
+__device__ __forceinline__ void umma_tmem_inner(uint32_t d_tmem, uint32_t a_tmem, uint64_t inner_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
 #pragma unroll
   for (int k = 0; k < kBI / 16; ++k)
-    umma_ts(d_tmem, a_tmem + k * 8, sdesc_sw128(inner + k * 2048, C::kInnerChunk, 1024), idesc,
-            (acc || k > 0) ? 1u : 0u);
+    umma_ts(d_tmem, a_tmem + k * 8, desc_add(inner_desc, k * 2048), idesc, (accumulate | k) ? 1u : 0u);
 }
 
 // ---------------------------------------------------------------------------- dK / dV
@@ -268,29 +267,38 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     __syncwarp();
   } else if (warp == kBwdWarpMma) {
     if (lane == 0) {
-      auto issue_sd = [&](int s) -> bool {
-        const int st = s % ST, bf = s & 1;
-        if (!mbar_wait(bar(BB_SFULL + st), (s / ST) & 1, p.status, kDevTimeoutBwd)) return false;
-        tc_fence_after();
-        const uint32_t sb = stage(st);
-        umma_outer_inner<D, C>(tmem + 256 + 128 * bf, sOA, sb + C::kStInA, IDESC_SD);       // S^T = K Q^T
-        umma_outer_inner<D, C>(tmem + 256 + 128 * bf + 64, sOB, sb + C::kStInB, IDESC_SD);  // dP^T = V dO^T
-        umma_commit(bar(BB_MFULL + bf));
-        return true;
-      };
-      bool ok = mbar_wait(bar(BB_OUTER), 0, p.status, kDevTimeoutBwd);
+      // descriptors: outer K / V (K-major), inner Q / dO of stage 0 as K-major (S^T, dP^T) and
+      // as MN-major B operands (dK, dV); stage st adds st * kStageBytes
+      const uint64_t dK_ = sdesc_sw128(sOA, 16, 1024), dV_ = sdesc_sw128(sOB, 16, 1024);
+      const uint64_t dQk = sdesc_sw128(stage(0) + C::kStInA, 16, 1024);
+      const uint64_t dOk = sdesc_sw128(stage(0) + C::kStInB, 16, 1024);
+      const uint64_t dQm = sdesc_sw128(stage(0) + C::kStInA, C::kInnerChunk, 1024);
+      const uint64_t dOm = sdesc_sw128(stage(0) + C::kStInB, C::kInnerChunk, 1024);
+      bool ok = mbar_wait(bar(BB_OUTER), 0, p.status, kDevTimeoutBwd) &&
+                mbar_wait(bar(BB_SFULL + 0), 0, p.status, kDevTimeoutBwd);
       if (ok) {
         tc_fence_after();
-        ok = issue_sd(0);
+        umma_outer_inner<D, C>(tmem + 256, dK_, dQk, IDESC_SD);       // S^T = K Q^T
+        umma_outer_inner<D, C>(tmem + 256 + 64, dV_, dOk, IDESC_SD);  // dP^T = V dO^T
+        umma_commit(bar(BB_MFULL + 0));
       }
       for (int s = 0; ok && s < nsteps; ++s) {
         const int st = s % ST, bf = s & 1;
-        if (s + 1 < nsteps && !(ok = issue_sd(s + 1))) break;
+        if (s + 1 < nsteps) {
+          const int st1 = (s + 1) % ST, bf1 = (s + 1) & 1;
+          if (!(ok = mbar_wait(bar(BB_SFULL + st1), ((s + 1) / ST) & 1, p.status, kDevTimeoutBwd))) break;
+          tc_fence_after();
+          const uint64_t so = static_cast<uint64_t>((st1 * C::kStageBytes) >> 4);
+          umma_outer_inner<D, C>(tmem + 256 + 128 * bf1, dK_, dQk + so, IDESC_SD);
+          umma_outer_inner<D, C>(tmem + 256 + 128 * bf1 + 64, dV_, dOk + so, IDESC_SD);
+          umma_commit(bar(BB_MFULL + bf1));
+        }
         if (!(ok = mbar_wait(bar(BB_PFULL + bf), (s >> 1) & 1, p.status, kDevTimeoutBwd))) break;
         tc_fence_after();
-        const uint32_t sb = stage(st);
-        umma_tmem_inner<D, C>(tmem + 0, tmem + 256 + 128 * bf, sb + C::kStInB, IDESC_ACC, s > 0);         // dV += P^T dO
-        umma_tmem_inner<D, C>(tmem + 128, tmem + 256 + 128 * bf + 64, sb + C::kStInA, IDESC_ACC, s > 0);  // dK += dS^T Q
+        const uint64_t so = static_cast<uint64_t>((st * C::kStageBytes) >> 4);
+        const uint32_t acc = s > 0 ? 1u : 0u;
+        umma_tmem_inner<D, C>(tmem + 0, tmem + 256 + 128 * bf, dOm + so, IDESC_ACC, acc);         // dV += P^T dO
+        umma_tmem_inner<D, C>(tmem + 128, tmem + 256 + 128 * bf + 64, dQm + so, IDESC_ACC, acc);  // dK += dS^T Q
         umma_commit(bar(BB_SEMPTY + st));
       }
       if (ok) umma_commit(bar(BB_ACC));
@@ -432,27 +440,33 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     __syncwarp();
   } else if (warp == kBwdWarpMma) {
     if (lane == 0) {
-      auto issue_sd = [&](int s) -> bool {
-        const int st = s % ST, bf = s & 1;
-        if (!mbar_wait(bar(BB_SFULL + st), (s / ST) & 1, p.status, kDevTimeoutBwd)) return false;
-        tc_fence_after();
-        const uint32_t sb = stage(st);
-        umma_outer_inner<D, C>(tmem + 256 + 128 * bf, sOA, sb + C::kStInA, IDESC_SD);       // S = Q K^T
-        umma_outer_inner<D, C>(tmem + 256 + 128 * bf + 64, sOB, sb + C::kStInB, IDESC_SD);  // dP = dO V^T
-        umma_commit(bar(BB_MFULL + bf));
-        return true;
-      };
-      bool ok = mbar_wait(bar(BB_OUTER), 0, p.status, kDevTimeoutBwd);
+      const uint64_t dQ_ = sdesc_sw128(sOA, 16, 1024), dO_ = sdesc_sw128(sOB, 16, 1024);
+      const uint64_t dKk = sdesc_sw128(stage(0) + C::kStInA, 16, 1024);
+      const uint64_t dVk = sdesc_sw128(stage(0) + C::kStInB, 16, 1024);
+      const uint64_t dKm = sdesc_sw128(stage(0) + C::kStInA, C::kInnerChunk, 1024);
+      bool ok = mbar_wait(bar(BB_OUTER), 0, p.status, kDevTimeoutBwd) &&
+                mbar_wait(bar(BB_SFULL + 0), 0, p.status, kDevTimeoutBwd);
       if (ok) {
         tc_fence_after();
-        ok = issue_sd(0);
+        umma_outer_inner<D, C>(tmem + 256, dQ_, dKk, IDESC_SD);       // S = Q K^T
+        umma_outer_inner<D, C>(tmem + 256 + 64, dO_, dVk, IDESC_SD);  // dP = dO V^T
+        umma_commit(bar(BB_MFULL + 0));
       }
       for (int s = 0; ok && s < nsteps; ++s) {
         const int st = s % ST, bf = s & 1;
-        if (s + 1 < nsteps && !(ok = issue_sd(s + 1))) break;
+        if (s + 1 < nsteps) {
+          const int st1 = (s + 1) % ST, bf1 = (s + 1) & 1;
+          if (!(ok = mbar_wait(bar(BB_SFULL + st1), ((s + 1) / ST) & 1, p.status, kDevTimeoutBwd))) break;
+          tc_fence_after();
+          const uint64_t so = static_cast<uint64_t>((st1 * C::kStageBytes) >> 4);
+          umma_outer_inner<D, C>(tmem + 256 + 128 * bf1, dQ_, dKk + so, IDESC_SD);
+          umma_outer_inner<D, C>(tmem + 256 + 128 * bf1 + 64, dO_, dVk + so, IDESC_SD);
+          umma_commit(bar(BB_MFULL + bf1));
+        }
         if (!(ok = mbar_wait(bar(BB_PFULL + bf), (s >> 1) & 1, p.status, kDevTimeoutBwd))) break;
         tc_fence_after();
-        umma_tmem_inner<D, C>(tmem + 0, tmem + 256 + 128 * bf + 64, stage(st) + C::kStInA, IDESC_ACC, s > 0);  // dQ += dS K
+        const uint64_t so = static_cast<uint64_t>((st * C::kStageBytes) >> 4);
+        umma_tmem_inner<D, C>(tmem + 0, tmem + 256 + 128 * bf + 64, dKm + so, IDESC_ACC, s > 0 ? 1u : 0u);  // dQ += dS K
         umma_commit(bar(BB_SEMPTY + st));
       }
       if (ok) umma_commit(bar(BB_ACC));

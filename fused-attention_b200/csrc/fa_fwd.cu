@@ -13,9 +13,12 @@
 // Warp roles (384 threads, warpgroup aligned):
 //   warps 0-3   softmax for tile 0 (one TMEM lane = one query row per thread)
 //   warps 4-7   softmax for tile 1
-//   warp 8      TMA producer: Q tiles once, then a K/V shared-memory ring
-//   warp 9      UMMA issuer: S_t = Q_t K_j^T into TMEM, O_t += P_t V_j with P_t read from TMEM
-//   warps 10-11 idle
+//   warp 8      TMA producer: Q tiles once, then the K ring (K(j) is freed once every tile's
+//               Q K^T has read it, well before V(j) is freed, so K loads run ahead)
+//   warp 9      UMMA issuer (one thread): S_t = Q_t K_j^T into TMEM, O_t += P_t V_j with P_t
+//               read from TMEM; descriptors are precomputed and advanced by constant offsets
+//   warp 10     TMA producer: the V ring
+//   warp 11     idle
 // TMEM (512 columns): S_0 | S_1 | O_0 | O_1, 128 columns each; P_t (16-bit) overwrites the first
 // half of S_t once the row has been read into registers.  The two softmax warpgroups ping-pong:
 // while one converts its S tile the tensor core runs the other tile's P V and next Q K^T.
@@ -28,8 +31,9 @@ namespace fa {
 namespace {
 
 constexpr int kThreads = 384;
-constexpr int kWarpProducer = 8;
+constexpr int kWarpProducerK = 8;   // Q tiles, then the K ring
 constexpr int kWarpMma = 9;
+constexpr int kWarpProducerV = 10;  // the V ring
 constexpr int kBM = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only if the max grows > 256x
@@ -40,29 +44,31 @@ struct FwdCfg {
   static constexpr int kQChunkBytes = kBM * 128;
   static constexpr int kKVChunkBytes = BN * 128;
   static constexpr int kQBytes = kBM * D * 2;
-  static constexpr int kKVBytes = BN * D * 2;
-  static constexpr int kStageBytes = 2 * kKVBytes;  // K tile + V tile
+  static constexpr int kKVBytes = BN * D * 2;       // one K (or V) tile
   static constexpr int kBudget = 225 * 1024;
-  static constexpr int kStagesFit = (kBudget - 2 * kQBytes - 1024) / kStageBytes;
-  static constexpr int kStages = kStagesFit > 4 ? 4 : kStagesFit;
-  static_assert(kStages >= 2, "need at least a double-buffered K/V ring");
+  static constexpr int kSlots = (kBudget - 2 * kQBytes) / kKVBytes;  // K + V ring slots that fit
+  static constexpr int kVStages = (kSlots / 2) > 4 ? 4 : (kSlots / 2);
+  static constexpr int kKStages = (kSlots - kVStages) > 4 ? 4 : (kSlots - kVStages);
+  static_assert(kVStages >= 2 && kKStages >= 2, "need double-buffered K and V rings");
   static constexpr int kOffQ = 0;
-  static constexpr int kOffKV = 2 * kQBytes;
-  static constexpr int kOffBar = kOffKV + kStages * kStageBytes;
+  static constexpr int kOffK = 2 * kQBytes;
+  static constexpr int kOffV = kOffK + kKStages * kKVBytes;
+  static constexpr int kOffBar = kOffV + kVStages * kKVBytes;
   static constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers + 1 KiB alignment slack
 };
 
 // barrier slots
 enum : int {
   BAR_Q = 0,
-  BAR_KFULL = 1,    // + stage (4)
-  BAR_VFULL = 5,    // + stage (4)
-  BAR_KVEMPTY = 9,  // + stage (4)
-  BAR_SFULL = 13,   // + tile (2)
-  BAR_PFULL = 15,   // + tile (2)
-  BAR_OFULL = 17,   // + tile (2)
-  BAR_DRAIN = 19,
-  BAR_COUNT = 20
+  BAR_KFULL = 1,    // + K stage (4)
+  BAR_KEMPTY = 5,   // + K stage (4)
+  BAR_VFULL = 9,    // + V stage (4)
+  BAR_VEMPTY = 13,  // + V stage (4)
+  BAR_SFULL = 17,   // + tile (2)
+  BAR_PFULL = 19,   // + tile (2)
+  BAR_OFULL = 21,   // + tile (2)
+  BAR_DRAIN = 23,
+  BAR_COUNT = 24
 };
 
 struct QTile {
@@ -111,14 +117,35 @@ __device__ __forceinline__ Work decode_work(const FwdParams& p, int item) {
   return w;
 }
 
+// S = Q K^T for one 128-row query tile: D/16 UMMAs, descriptors advanced by constant offsets.
+template <int D, int BN, bool BF16>
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint64_t q_desc, uint64_t k_desc) {
+  using C = FwdCfg<D, BN>;
+  constexpr uint32_t IDESC = idesc_f16(BF16, kBM, BN, false, false);  // Q, K both K-major
+#pragma unroll
+  for (int k = 0; k < D / 16; ++k) {
+    umma_ss(d_tmem, desc_add(q_desc, (k / 4) * C::kQChunkBytes + (k % 4) * 32),
+            desc_add(k_desc, (k / 4) * C::kKVChunkBytes + (k % 4) * 32), IDESC, k > 0 ? 1u : 0u);
+  }
+}
+
+// O += P V: P (16-bit) read from TMEM as the A operand, V MN-major in shared memory.
+template <int D, int BN, bool BF16>
+__device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint64_t v_desc,
+                                         uint32_t accumulate) {
+  constexpr uint32_t IDESC = idesc_f16(BF16, kBM, D, false, true);
+#pragma unroll
+  for (int k = 0; k < BN / 16; ++k)
+    umma_ts(o_tmem, p_tmem + k * 8, desc_add(v_desc, k * 2048), IDESC, (accumulate | k) ? 1u : 0u);
+}
+
 template <int D, int BN, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
   using C = FwdCfg<D, BN>;
-  constexpr int ST = C::kStages;
-  constexpr uint32_t IDESC_S = idesc_f16(BF16, kBM, BN, false, false);  // Q, K both K-major
-  constexpr uint32_t IDESC_O = idesc_f16(BF16, kBM, D, false, true);    // P (TMEM), V MN-major
+  constexpr int KST = C::kKStages;
+  constexpr int VST = C::kVStages;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -127,9 +154,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + C::kOffBar + 8 * BAR_COUNT);
   volatile int* abort_slot = reinterpret_cast<volatile int*>(smem + C::kOffBar + 8 * BAR_COUNT + 4);
-  auto bar = [&](int i) -> uint32_t { return smem_u32(bars + i); };
+  const uint32_t bar0 = smem_u32(bars);
+#define BAR(i) (bar0 + 8u * static_cast<uint32_t>(i))
   const uint32_t sQ = base + C::kOffQ;
-  const uint32_t sKV = base + C::kOffKV;
+  const uint32_t sK = base + C::kOffK;
+  const uint32_t sV = base + C::kOffV;
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -146,18 +175,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
-    mbar_init(bar(BAR_Q), 1);
+    mbar_init(BAR(BAR_Q), 1);
     for (int s = 0; s < 4; ++s) {
-      mbar_init(bar(BAR_KFULL + s), 1);
-      mbar_init(bar(BAR_VFULL + s), 1);
-      mbar_init(bar(BAR_KVEMPTY + s), 1);
+      mbar_init(BAR(BAR_KFULL + s), 1);
+      mbar_init(BAR(BAR_KEMPTY + s), 1);
+      mbar_init(BAR(BAR_VFULL + s), 1);
+      mbar_init(BAR(BAR_VEMPTY + s), 1);
     }
     for (int t = 0; t < 2; ++t) {
-      mbar_init(bar(BAR_SFULL + t), 1);
-      mbar_init(bar(BAR_PFULL + t), 128);
-      mbar_init(bar(BAR_OFULL + t), 1);
+      mbar_init(BAR(BAR_SFULL + t), 1);
+      mbar_init(BAR(BAR_PFULL + t), 128);
+      mbar_init(BAR(BAR_OFULL + t), 1);
     }
-    mbar_init(bar(BAR_DRAIN), 1);
+    mbar_init(BAR(BAR_DRAIN), 1);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -169,104 +199,118 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == kWarpProducer) {
-    // ------------------------------------------------------------ TMA producer
+  if (warp == kWarpProducerK) {
+    // ------------------------------------------------------------ TMA: Q once, then the K ring
     if (lane == 0) {
       const uint64_t pol_q = policy_evict_first();
       const uint64_t pol_kv = policy_evict_last();
-      mbar_arrive_expect_tx(bar(BAR_Q), w.ntiles * C::kQBytes);
+      mbar_arrive_expect_tx(BAR(BAR_Q), w.ntiles * C::kQBytes);
       for (int t = 0; t < w.ntiles; ++t)
         for (int c = 0; c < C::kChunks; ++c)
-          tma_load_3d(sQ + t * C::kQBytes + c * C::kQChunkBytes, &tmQ, bar(BAR_Q), c * 64,
+          tma_load_3d(sQ + t * C::kQBytes + c * C::kQChunkBytes, &tmQ, BAR(BAR_Q), c * 64,
                       w.t[t].qt * kBM, w.t[t].bh, pol_q);
       int issued = 0;
       for (int j = 0; j < nmax; ++j) {
-        const int s = j % ST;
-        const uint32_t ph = (j / ST) & 1;
-        if (!mbar_wait(bar(BAR_KVEMPTY + s), ph ^ 1, p.status, kDevTimeoutKVEmpty)) break;
-        const uint32_t sK = sKV + s * C::kStageBytes;
-        const uint32_t sV = sK + C::kKVBytes;
-        mbar_arrive_expect_tx(bar(BAR_KFULL + s), C::kKVBytes);
+        const int s = j % KST;
+        if (!mbar_wait(BAR(BAR_KEMPTY + s), ((j / KST) & 1) ^ 1, p.status, kDevTimeoutKVEmpty)) break;
+        mbar_arrive_expect_tx(BAR(BAR_KFULL + s), C::kKVBytes);
         for (int c = 0; c < C::kChunks; ++c)
-          tma_load_3d(sK + c * C::kKVChunkBytes, &tmK, bar(BAR_KFULL + s), c * 64, j * BN,
-                      w.bh_kv, pol_kv);
-        mbar_arrive_expect_tx(bar(BAR_VFULL + s), C::kKVBytes);
-        for (int c = 0; c < C::kChunks; ++c)
-          tma_load_3d(sV + c * C::kKVChunkBytes, &tmV, bar(BAR_VFULL + s), c * 64, j * BN,
-                      w.bh_kv, pol_kv);
+          tma_load_3d(sK + s * C::kKVBytes + c * C::kKVChunkBytes, &tmK, BAR(BAR_KFULL + s), c * 64,
+                      j * BN, w.bh_kv, pol_kv);
         ++issued;
       }
       // Never leave the CTA with a copy still writing into shared memory.
-      drain_wait(bar(BAR_Q), 0, p.status);
-      for (int j = max(0, issued - ST); j < issued; ++j) {
-        drain_wait(bar(BAR_KFULL + j % ST), (j / ST) & 1, p.status);
-        drain_wait(bar(BAR_VFULL + j % ST), (j / ST) & 1, p.status);
+      drain_wait(BAR(BAR_Q), 0, p.status);
+      for (int j = max(0, issued - KST); j < issued; ++j)
+        drain_wait(BAR(BAR_KFULL + j % KST), (j / KST) & 1, p.status);
+    }
+    __syncwarp();
+  } else if (warp == kWarpProducerV) {
+    // ------------------------------------------------------------ TMA: the V ring
+    if (lane == 0) {
+      const uint64_t pol_kv = policy_evict_last();
+      int issued = 0;
+      for (int j = 0; j < nmax; ++j) {
+        const int s = j % VST;
+        if (!mbar_wait(BAR(BAR_VEMPTY + s), ((j / VST) & 1) ^ 1, p.status, kDevTimeoutKVEmpty)) break;
+        mbar_arrive_expect_tx(BAR(BAR_VFULL + s), C::kKVBytes);
+        for (int c = 0; c < C::kChunks; ++c)
+          tma_load_3d(sV + s * C::kKVBytes + c * C::kKVChunkBytes, &tmV, BAR(BAR_VFULL + s), c * 64,
+                      j * BN, w.bh_kv, pol_kv);
+        ++issued;
       }
+      for (int j = max(0, issued - VST); j < issued; ++j)
+        drain_wait(BAR(BAR_VFULL + j % VST), (j / VST) & 1, p.status);
     }
     __syncwarp();
   } else if (warp == kWarpMma) {
-    // ------------------------------------------------------------ UMMA issuer
+    // ------------------------------------------------------------ UMMA issuer (one thread)
     if (lane == 0) {
-      auto issue_s = [&](int t, int s) {
-        const uint32_t qa = sQ + t * C::kQBytes;
-        const uint32_t kb = sKV + s * C::kStageBytes;
-#pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (k % 4) * 32;  // 16 elements = 32 B inside the 128-B row
-          const uint64_t ad = sdesc_sw128(qa + (k / 4) * C::kQChunkBytes + off, 16, 1024);
-          const uint64_t bd = sdesc_sw128(kb + (k / 4) * C::kKVChunkBytes + off, 16, 1024);
-          umma_ss(tmem + t * 128, ad, bd, IDESC_S, k > 0 ? 1u : 0u);
-        }
-      };
-      auto issue_pv = [&](int t, int s, bool acc) {
-        const uint32_t vb = sKV + s * C::kStageBytes + C::kKVBytes;
-#pragma unroll
-        for (int k = 0; k < BN / 16; ++k) {
-          const uint64_t bd = sdesc_sw128(vb + k * 2048, C::kKVChunkBytes, 1024);
-          umma_ts(tmem + 256 + t * 128, tmem + t * 128 + k * 8, bd, IDESC_O,
-                  (acc || k > 0) ? 1u : 0u);
-        }
-      };
-      bool ok = mbar_wait(bar(BAR_Q), 0, p.status, kDevTimeoutQ) &&
-                mbar_wait(bar(BAR_KFULL + 0), 0, p.status, kDevTimeoutKV);
+      const uint64_t dq0 = sdesc_sw128(sQ, 16, 1024);
+      const uint64_t dq1 = sdesc_sw128(sQ + C::kQBytes, 16, 1024);
+      const uint64_t dk0 = sdesc_sw128(sK, 16, 1024);
+      const uint64_t dv0 = sdesc_sw128(sV, C::kKVChunkBytes, 1024);
+      const uint32_t tS0 = tmem, tS1 = tmem + 128, tO0 = tmem + 256, tO1 = tmem + 384;
+      const int n0 = w.nkv[0], n1 = w.nkv[1];
+      bool ok = mbar_wait(BAR(BAR_Q), 0, p.status, kDevTimeoutQ) &&
+                mbar_wait(BAR(BAR_KFULL + 0), 0, p.status, kDevTimeoutKV);
       if (ok) {
         tc_fence_after();
-        for (int t = 0; t < w.ntiles; ++t) {
-          issue_s(t, 0);
-          umma_commit(bar(BAR_SFULL + t));
+        issue_qk<D, BN, BF16>(tS0, dq0, dk0);
+        umma_commit(BAR(BAR_SFULL + 0));
+        if (n1 > 0) {
+          issue_qk<D, BN, BF16>(tS1, dq1, dk0);
+          umma_commit(BAR(BAR_SFULL + 1));
         }
+        umma_commit(BAR(BAR_KEMPTY + 0));
       }
       for (int j = 0; ok && j < nmax; ++j) {
-        const int s = j % ST;
-        ok = mbar_wait(bar(BAR_VFULL + s), (j / ST) & 1, p.status, kDevTimeoutKV);
-        if (!ok) break;
-        tc_fence_after();
-        bool next_k_ready = false;
-        const int s1 = (j + 1) % ST;
-        for (int t = 0; t < w.ntiles && ok; ++t) {
-          if (j >= w.nkv[t]) continue;
-          ok = mbar_wait(bar(BAR_PFULL + t), j & 1, p.status, kDevTimeoutP);
-          if (!ok) break;
+        const int vs = j % VST;
+        const int ks1 = (j + 1) % KST;
+        const uint64_t dvj = dv0 + static_cast<uint64_t>((vs * C::kKVBytes) >> 4);
+        const uint64_t dkn = dk0 + static_cast<uint64_t>((ks1 * C::kKVBytes) >> 4);
+        if (!(ok = mbar_wait(BAR(BAR_VFULL + vs), (j / VST) & 1, p.status, kDevTimeoutKV))) break;
+        bool k_ready = false;
+        bool issued_s = false;
+        // tile 0
+        if (j < n0) {
+          if (!(ok = mbar_wait(BAR(BAR_PFULL + 0), j & 1, p.status, kDevTimeoutP))) break;
           tc_fence_after();
-          issue_pv(t, s, j > 0);
-          if (j + 1 == w.nkv[t]) {
-            umma_commit(bar(BAR_OFULL + t));
+          issue_pv<D, BN, BF16>(tO0, tS0, dvj, j > 0 ? 1u : 0u);
+          if (j + 1 == n0) {
+            umma_commit(BAR(BAR_OFULL + 0));
           } else {
-            if (!next_k_ready) {
-              ok = mbar_wait(bar(BAR_KFULL + s1), ((j + 1) / ST) & 1, p.status, kDevTimeoutKV);
-              if (!ok) break;
-              tc_fence_after();
-              next_k_ready = true;
-            }
-            issue_s(t, s1);
-            umma_commit(bar(BAR_SFULL + t));
+            if (!(ok = mbar_wait(BAR(BAR_KFULL + ks1), ((j + 1) / KST) & 1, p.status, kDevTimeoutKV))) break;
+            tc_fence_after();
+            k_ready = true;
+            issue_qk<D, BN, BF16>(tS0, dq0, dkn);
+            umma_commit(BAR(BAR_SFULL + 0));
+            issued_s = true;
           }
         }
-        umma_commit(bar(BAR_KVEMPTY + s));
+        // tile 1
+        if (j < n1) {
+          if (!(ok = mbar_wait(BAR(BAR_PFULL + 1), j & 1, p.status, kDevTimeoutP))) break;
+          tc_fence_after();
+          issue_pv<D, BN, BF16>(tO1, tS1, dvj, j > 0 ? 1u : 0u);
+          if (j + 1 == n1) {
+            umma_commit(BAR(BAR_OFULL + 1));
+          } else {
+            if (!k_ready) {
+              if (!(ok = mbar_wait(BAR(BAR_KFULL + ks1), ((j + 1) / KST) & 1, p.status, kDevTimeoutKV))) break;
+              tc_fence_after();
+            }
+            issue_qk<D, BN, BF16>(tS1, dq1, dkn);
+            umma_commit(BAR(BAR_SFULL + 1));
+            issued_s = true;
+          }
+        }
+        if (issued_s) umma_commit(BAR(BAR_KEMPTY + ks1));  // K(j+1) read by every tile that needs it
+        umma_commit(BAR(BAR_VEMPTY + vs));                 // V(j) read by every tile that needs it
       }
       // All MMAs issued by this thread must finish before TMEM is released.
-      umma_commit(bar(BAR_DRAIN));
-      drain_wait(bar(BAR_DRAIN), 0, p.status);
+      umma_commit(BAR(BAR_DRAIN));
+      drain_wait(BAR(BAR_DRAIN), 0, p.status);
     }
     __syncwarp();
   } else if (warp < 8) {
@@ -286,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float l = 0.f;
       bool ok = true;
       for (int j = 0; j < nkv; ++j) {
-        ok = mbar_wait(bar(BAR_SFULL + t), j & 1, p.status, kDevTimeoutS);
+        ok = mbar_wait(BAR(BAR_SFULL + t), j & 1, p.status, kDevTimeoutS);
         if (!ok) break;
         tc_fence_after();
         uint32_t r[BN / 32][32];
@@ -304,17 +348,24 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (key > qrow || key >= p.S) r[c][i] = __float_as_uint(-INFINITY);
             }
         }
-        float mx = -INFINITY;
+        // row max with 8 independent partial maxima (short dependency chains)
+        float mx8[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mx8[u] = -INFINITY;
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(r[c][i]));
+          for (int i = 0; i < 32; ++i) mx8[i % 8] = fmaxf(mx8[i % 8], __uint_as_float(r[c][i]));
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         const float mt = mx * scale;
         const bool upd = mt > m_used + kRescaleThreshold;
         const float m_new = upd ? mt : m_used;
         const float alpha = ex2_approx(m_used - m_new);
         const float neg_m = -m_new;
-        float sum = 0.f;
+        float sum8[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) sum8[u] = 0.f;
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t pk[16];
@@ -322,11 +373,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 16; ++i) {
             const float p0 = ex2_approx(fmaf(__uint_as_float(r[c][2 * i]), scale, neg_m));
             const float p1 = ex2_approx(fmaf(__uint_as_float(r[c][2 * i + 1]), scale, neg_m));
-            sum += p0 + p1;
+            sum8[(2 * i) % 8] += p0;
+            sum8[(2 * i + 1) % 8] += p1;
             pk[i] = pack2<BF16>(p0, p1);
           }
           tmem_st16(tS + c * 16, pk);
         }
+        const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
         l = l * alpha + sum;
         m_used = m_new;
         // Rescale the running O of this warp's rows if any row's max moved (P V of tile j-1 is
@@ -344,9 +397,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(bar(BAR_PFULL + t));
+        mbar_arrive(BAR(BAR_PFULL + t));
       }
-      if (ok) ok = mbar_wait(bar(BAR_OFULL + t), 0, p.status, kDevTimeoutO);
+      if (ok) ok = mbar_wait(BAR(BAR_OFULL + t), 0, p.status, kDevTimeoutO);
       if (ok) {
         tc_fence_after();
         const float inv_l = 1.0f / l;
@@ -374,6 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+#undef BAR
 
   tc_fence_before();
   __syncthreads();

@@ -98,8 +98,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Wait until the phase with the given parity has completed.  Returns false (after recording
 // `code` in the status word, unless another CTA already failed) if the wait exceeds
 // FA_WAIT_TIMEOUT_NS or if the status word shows that some CTA has already failed.
-static __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* status, int code) {
-  if (mbar_try_wait(bar, parity)) return true;
+// The already-complete case is inlined; only a real wait calls the polling loop.
+static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, int* status,
+                                                   int code) {
   const uint64_t t0 = global_timer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -111,6 +112,11 @@ static __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int
       }
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* status, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, status, code);
 }
 
 // Bounded wait used only while tearing down: ignores the abort flag so that copies and MMAs
@@ -207,6 +213,13 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, ui
   return d;
 }
 
+// Advance a descriptor's start address by `bytes` (a multiple of 16).  The start-address field
+// is the low 14 bits of (address >> 4); shared-memory addresses stay below 256 KiB, so the add
+// never carries into the next field.
+__device__ __forceinline__ uint64_t desc_add(uint64_t desc, uint32_t bytes) {
+  return desc + static_cast<uint64_t>(bytes >> 4);
+}
+
 // Instruction descriptor for kind::f16 with an fp32 accumulator.
 //   [4,6) D format (1 = f32), [7,10) A format, [10,13) B format (0 = f16, 1 = bf16),
 //   [15] A major (0 = K, 1 = MN), [16] B major, [17,23) N >> 3, [24,29) M >> 4.
@@ -224,8 +237,7 @@ __device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
 // D[tmem] (+)= A[tmem] * B[smem desc]   (A read from TMEM, K-major, 2 x 16-bit per column)
@@ -235,8 +247,7 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
 // Arrive (once) on an mbarrier when every tcgen05 op previously issued by this thread is done.
