@@ -210,7 +210,7 @@ int fa_bwd_dkdv(const void* q, const void* k, const void* v, const void* dO, con
   CUtensorMap tmQ, tmK, tmV, tmdO;
   fa::BwdParams p{};
   int rc = bwd_prepare(q, k, v, dO, lse, delta, B, H, H_kv, S, D, dtype, tile_m, tile_n,
-                       dev_status, &tmQ, &tmK, &tmV, &tmdO, &p, /*q_rows=*/64, /*kv_rows=*/128);
+                       dev_status, &tmQ, &tmK, &tmV, &tmdO, &p, /*q_rows=*/128, /*kv_rows=*/128);
   if (rc != FA_OK) return rc;
   p.dk = dk;
   p.dv = dv;
@@ -227,7 +227,7 @@ int fa_bwd_dq(const void* q, const void* k, const void* v, const void* dO, const
   CUtensorMap tmQ, tmK, tmV, tmdO;
   fa::BwdParams p{};
   int rc = bwd_prepare(q, k, v, dO, lse, delta, B, H, H_kv, S, D, dtype, tile_m, tile_n,
-                       dev_status, &tmQ, &tmK, &tmV, &tmdO, &p, /*q_rows=*/128, /*kv_rows=*/64);
+                       dev_status, &tmQ, &tmK, &tmV, &tmdO, &p, /*q_rows=*/128, /*kv_rows=*/128);
   if (rc != FA_OK) return rc;
   p.dq = dq;
   cudaError_t e = fa::launch_bwd_dq(tmQ, tmK, tmV, tmdO, p, dtype == FA_DTYPE_BF16,

@@ -51,124 +51,45 @@ cudaError_t launch_pre_t(const BwdParams& p, cudaStream_t stream) {
 }
 
 // ============================================================================ dK/dV and dQ
-// Shared structure of the two atomic-free backward kernels.  A CTA keeps one 128-row OUTER tile
-// resident in shared memory and streams 64-row INNER tiles through a TMA ring:
-//   dK/dV: outer = 128 keys (K, V) of one K/V head; inner = 64-query tiles (Q, dO, lse, delta)
-//          of every query head of the GQA group, for the query tiles that see those keys
-//          (reference loop: attention/backward/fused_backward.py:81-103)
-//   dQ:    outer = 128 queries (Q, dO) of one head; inner = 64-key tiles (K, V) up to the
-//          diagonal (reference loop: attention/backward/fused_backward.py:128-144)
-// Warp roles (384 threads): warps 0-3 / 4-7 = two compute warpgroups that take alternate inner
-// steps, warp 8 = TMA producer, warp 9 = UMMA issuer.  TMEM (512 columns):
-//   [0, D)            dV   (dK/dV kernel) | dQ (dQ kernel)
-//   [128, 128 + D)    dK   (dK/dV kernel)
-//   256 + 128 b       buffer b in {0, 1}: 64 columns of S (or S^T), then 64 columns of dP (dP^T).
-// P^T (16-bit) overwrites the first 32 columns of S^T and dS (dS^T) the first 32 of dP (dP^T)
-// once a thread has read its row, and feed the next UMMAs straight from TMEM.  While one
-// warpgroup turns buffer b into P/dS, the tensor core computes the other buffer's S/dP and the
-// previous step's accumulations, so neither side waits for the other in steady state.
+// Two atomic-free backward kernels on 128 x 128 tiles (every UMMA is M=128, N=128 or N=D).
+//   dQ:    CTA = 128 query rows of one head (Q, dO resident); streams 128-key K and V tiles up
+//          to the diagonal (reference loop: attention/backward/fused_backward.py:128-144).
+//          TMEM: dQ | S | dP[0] | dP[1].  S is released as soon as both compute warpgroups have
+//          read it, so S(s+1) runs on the tensor core while P(s) is being computed; dS overwrites
+//          the first half of each warpgroup's own dP columns and feeds dQ += dS K from TMEM.
+//   dK/dV: CTA = 128 keys of one K/V head (K, V resident); streams 128-row Q / dO tiles (and
+//          their LSE / delta slices) of every query head of the GQA group, from the diagonal on
+//          (reference loop: attention/backward/fused_backward.py:81-103).
+//          TMEM: dV | dK | S^T | dP^T.  S^T is released on read; P^T goes to shared memory in
+//          the 128-byte-swizzled K-major layout the tensor core reads as an A operand, so the next
+//          S^T overlaps the exp work; dS^T overwrites dP^T and feeds dK += dS^T Q from TMEM.
+// Warp roles (384 threads): warps 0-3 and 4-7 are two compute warpgroups splitting every tile's
+// 128 columns (each thread: one TMEM lane = one row, 64 columns); warp 8 (and 10 in dQ) issue TMA
+// loads; warp 9 is the single-thread UMMA issuer.  All warps run with the launch allocation of
+// 168 registers per thread.
 constexpr int kBwdThreads = 384;
-constexpr int kBwdWarpProducer = 8;
+constexpr int kBwdWarpLoadA = 8;
 constexpr int kBwdWarpMma = 9;
-constexpr int kBO = 128;  // outer tile rows
-constexpr int kBI = 64;   // inner tile rows
+constexpr int kBwdWarpLoadB = 10;
+constexpr int kBT = 128;  // tile rows (outer and inner)
 constexpr uint32_t kBwdTmemCols = 512;
+constexpr int kSmemOptin = 232448;  // max dynamic shared memory per block on sm_100
 
-template <int D>
-struct BwdCfg {
-  static constexpr int kChunks = D / 64;
-  static constexpr int kOuterChunk = kBO * 128;
-  static constexpr int kInnerChunk = kBI * 128;
-  static constexpr int kOuterBytes = kBO * D * 2;
-  static constexpr int kInnerBytes = kBI * D * 2;
-  static constexpr int kStatBytes = kBI * 4;
-  static constexpr int kStageBytes = ((2 * kInnerBytes + 2 * kStatBytes) + 1023) / 1024 * 1024;
-  static constexpr int kBudget = 225 * 1024;
-  static constexpr int kStagesFit = (kBudget - 2 * kOuterBytes - 1024) / kStageBytes;
-  static constexpr int kStages = kStagesFit > 4 ? 4 : kStagesFit;
-  static_assert(kStages >= 2, "need a double-buffered inner ring");
-  static constexpr int kOffOuterA = 0;              // K (dK/dV) or Q (dQ)
-  static constexpr int kOffOuterB = kOuterBytes;    // V (dK/dV) or dO (dQ)
-  static constexpr int kOffStages = 2 * kOuterBytes;
-  // inside a stage: inner A (Q | K), inner B (dO | V), lse slice, delta slice
-  static constexpr int kStInA = 0;
-  static constexpr int kStInB = kInnerBytes;
-  static constexpr int kStLse = 2 * kInnerBytes;
-  static constexpr int kStDelta = 2 * kInnerBytes + kStatBytes;
-  static constexpr int kOffBar = kOffStages + kStages * kStageBytes;
-  static constexpr int kSmemBytes = kOffBar + 256 + 1024;
-};
-
-enum : int {
-  BB_OUTER = 0,
-  BB_SFULL = 1,   // + stage (4)
-  BB_SEMPTY = 5,  // + stage (4)
-  BB_MFULL = 9,   // + buffer (2): S / dP of a step are in TMEM
-  BB_PFULL = 11,  // + buffer (2): P / dS of a step are in TMEM
-  BB_ACC = 13,
-  BB_DRAIN = 14,
-  BB_COUNT = 15
-};
-
-struct BwdSmem {
-  uint32_t base;
-  uint8_t* ptr;
-  uint64_t* bars;
-  volatile uint32_t* tmem_slot;
-  volatile int* abort_slot;
-};
-
-template <class C>
-__device__ __forceinline__ BwdSmem bwd_smem() {
-  extern __shared__ uint8_t smem_raw[];
-  BwdSmem s;
-  const uint32_t raw = smem_u32(smem_raw);
-  s.base = (raw + 1023u) & ~1023u;
-  s.ptr = smem_raw + (s.base - raw);
-  s.bars = reinterpret_cast<uint64_t*>(s.ptr + C::kOffBar);
-  s.tmem_slot = reinterpret_cast<volatile uint32_t*>(s.ptr + C::kOffBar + 8 * BB_COUNT);
-  s.abort_slot = reinterpret_cast<volatile int*>(s.ptr + C::kOffBar + 8 * BB_COUNT + 4);
-  return s;
-}
-
-// Common prologue: abort check, barrier init, TMEM allocation.  Returns false if this CTA
-// must stop because an earlier CTA already failed (uniform across the CTA).
-template <class C>
-__device__ __forceinline__ bool bwd_setup(const BwdSmem& sm, const BwdParams& p, uint32_t& tmem) {
-  if (threadIdx.x == 0) *sm.abort_slot = ld_status(p.status);
-  __syncthreads();
-  if (*sm.abort_slot != 0) return false;
-  if (threadIdx.x == 0) {
-    mbar_init(smem_u32(sm.bars + BB_OUTER), 1);
-    for (int s = 0; s < 4; ++s) {
-      mbar_init(smem_u32(sm.bars + BB_SFULL + s), 1);
-      mbar_init(smem_u32(sm.bars + BB_SEMPTY + s), 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(sm.bars + BB_MFULL + b), 1);
-      mbar_init(smem_u32(sm.bars + BB_PFULL + b), 128);
-    }
-    mbar_init(smem_u32(sm.bars + BB_ACC), 1);
-    mbar_init(smem_u32(sm.bars + BB_DRAIN), 1);
-    fence_barrier_init();
-  }
-  if (threadIdx.x / 32 == 0) {
-    tmem_alloc(smem_u32(const_cast<uint32_t*>(sm.tmem_slot)), kBwdTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  tmem = *sm.tmem_slot;
-  return true;
-}
-
-__device__ __forceinline__ void bwd_teardown(uint32_t tmem) {
-  tc_fence_before();
-  __syncthreads();
-  if (threadIdx.x / 32 == 0) {
-    tc_fence_after();
-    tmem_dealloc(tmem, kBwdTmemCols);
+// P = 2^(s * scale - m) for 64 values (m given per pair), fp32 results; 6 of every 16 pairs on
+// the FMA-pipe polynomial, the rest on MUFU ex2.
+template <int kN>
+__device__ __forceinline__ void exp2_row(const uint32_t* s, const float* neg_m, float scale, float* out) {
+  const uint64_t scale2 = f2(scale, scale);
+#pragma unroll
+  for (int i = 0; i < kN / 2; ++i) {
+    const uint64_t x2 = ffma2(f2u(s[2 * i], s[2 * i + 1]), scale2, f2(neg_m[2 * i], neg_m[2 * i + 1]));
+    uint64_t p2;
+    if ((0x5252u >> (i & 15)) & 1u)
+      p2 = exp2_poly2(f2lo(x2), f2hi(x2));
+    else
+      p2 = f2(ex2_approx(f2lo(x2)), ex2_approx(f2hi(x2)));
+    out[2 * i] = f2lo(p2);
+    out[2 * i + 1] = f2hi(p2);
   }
 }
 
@@ -184,193 +105,545 @@ __device__ __forceinline__ void store_row_chunk(uint8_t* dst, const uint32_t (&v
   for (int q = 0; q < 4; ++q) d[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
 }
 
-// Issue an M=128, N=64, K=D product of two K-major SW128 tiles (outer rows x inner rows);
-// descriptors are precomputed bases advanced by constant offsets.
-template <int D, class C>
-__device__ __forceinline__ void umma_outer_inner(uint32_t d_tmem, uint64_t outer_desc,
-                                                 uint64_t inner_desc, uint32_t idesc) {
+// D[128 x 128] (+)= A[128 x D] * B[128 x D]^T, both K-major SW128 tiles of 128 rows.
+template <int D, bool BF16>
+__device__ __forceinline__ void umma_rows_rows(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc) {
+  constexpr uint32_t IDESC = idesc_f16(BF16, kBT, kBT, false, false);
 #pragma unroll
   for (int k = 0; k < D / 16; ++k) {
-    umma_ss(d_tmem, desc_add(outer_desc, (k / 4) * C::kOuterChunk + (k % 4) * 32),
-            desc_add(inner_desc, (k / 4) * C::kInnerChunk + (k % 4) * 32), idesc, k > 0 ? 1u : 0u);
+    const uint32_t off = (k / 4) * (kBT * 128) + (k % 4) * 32;
+    umma_ss(d_tmem, desc_add(a_desc, off), desc_add(b_desc, off), IDESC, k > 0 ? 1u : 0u);
   }
 }
 
-// acc[128 x D] (+)= A[128 x 64] (16-bit, in TMEM) * B[64 x D] (inner tile, MN-major SW128).
-template <int D, class C>
-__device__ __forceinline__ void umma_tmem_inner(uint32_t d_tmem, uint32_t a_tmem, uint64_t inner_desc,
-                                                uint32_t idesc, uint32_t accumulate) {
+// acc[128 x D] (+)= A[128 x 128] (16-bit in TMEM, K-major) * B[128 x D] (MN-major SW128 tile).
+// A is stored in two halves, one per compute warpgroup: K columns 0-63 packed in TMEM columns
+// [a, a + 32), K columns 64-127 in [a + 64, a + 96) (each warpgroup writes into the first half of
+// its own column range, so it never overwrites values the other warpgroup has yet to read).
+template <int D, bool BF16>
+__device__ __forceinline__ void umma_tmem_tile(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t acc) {
+  constexpr uint32_t IDESC = idesc_f16(BF16, kBT, D, false, true);
 #pragma unroll
-  for (int k = 0; k < kBI / 16; ++k)
-    umma_ts(d_tmem, a_tmem + k * 8, desc_add(inner_desc, k * 2048), idesc, (accumulate | k) ? 1u : 0u);
+  for (int k = 0; k < kBT / 16; ++k)
+    umma_ts(d_tmem, a_tmem + (k / 4) * 64 + (k % 4) * 8, desc_add(b_desc, k * 2048), IDESC, (acc | k) ? 1u : 0u);
+}
+
+// acc[128 x D] (+)= A[128 x 128] (K-major SW128 in shared memory) * B[128 x D] (MN-major SW128).
+template <int D, bool BF16>
+__device__ __forceinline__ void umma_smem_tile(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t acc) {
+  constexpr uint32_t IDESC = idesc_f16(BF16, kBT, D, false, true);
+#pragma unroll
+  for (int k = 0; k < kBT / 16; ++k)
+    umma_ss(d_tmem, desc_add(a_desc, (k / 4) * (kBT * 128) + (k % 4) * 32), desc_add(b_desc, k * 2048),
+            IDESC, (acc | k) ? 1u : 0u);
+}
+
+struct BwdSmem {
+  uint32_t base;
+  uint8_t* ptr;
+  uint32_t bar0;
+  volatile uint32_t* tmem_slot;
+  volatile int* abort_slot;
+};
+
+// Aligns the working area to 1 KiB inside the dynamic allocation; `ok` is false if the
+// allocation's start leaves too little slack (never expected: the start is 1 KiB aligned).
+template <int kUsed>
+__device__ __forceinline__ BwdSmem bwd_smem(bool& ok) {
+  extern __shared__ uint8_t smem_raw[];
+  BwdSmem s;
+  const uint32_t raw = smem_u32(smem_raw);
+  s.base = (raw + 1023u) & ~1023u;
+  ok = (s.base - raw) + kUsed <= static_cast<uint32_t>(kSmemOptin);
+  s.ptr = smem_raw + (s.base - raw);
+  s.bar0 = s.base + kUsed - 256;
+  s.tmem_slot = reinterpret_cast<volatile uint32_t*>(s.ptr + kUsed - 256 + 8 * 28);
+  s.abort_slot = reinterpret_cast<volatile int*>(s.ptr + kUsed - 256 + 8 * 28 + 4);
+  return s;
+}
+
+// Common prologue: abort check, TMEM allocation.  Returns false (uniformly) if the CTA must stop.
+__device__ __forceinline__ bool bwd_setup(const BwdSmem& sm, bool smem_ok, const BwdParams& p, uint32_t& tmem) {
+  if (threadIdx.x == 0) {
+    int st = ld_status(p.status);
+    if (st == 0 && !smem_ok) {
+      record_error(p.status, kDevSmemLayout, 0);
+      st = kDevSmemLayout;
+    }
+    *sm.abort_slot = st;
+  }
+  __syncthreads();
+  if (*sm.abort_slot != 0) return false;
+  if (threadIdx.x / 32 == 0) {
+    tmem_alloc(smem_u32(const_cast<uint32_t*>(sm.tmem_slot)), kBwdTmemCols);
+    tmem_relinquish();
+  }
+  return true;
+}
+
+__device__ __forceinline__ void bwd_teardown(uint32_t tmem) {
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x / 32 == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kBwdTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------- dQ
+template <int D>
+struct DqCfg {
+  static constexpr int kTile = kBT * D * 2;
+  static constexpr int kBudget = kSmemOptin - 1024 - 256;
+  static constexpr int kSlots = (kBudget - 2 * kTile) / kTile;
+  static constexpr int kVStages = (kSlots / 2) > 4 ? 4 : (kSlots / 2);
+  static constexpr int kKStages = (kSlots - kVStages) > 4 ? 4 : (kSlots - kVStages);
+  static_assert(kKStages >= 2 && kVStages >= 2, "need double-buffered K and V rings");
+  static constexpr int kOffQ = 0, kOffdO = kTile, kOffK = 2 * kTile;
+  static constexpr int kOffV = kOffK + kKStages * kTile;
+  static constexpr int kUsed = kOffV + kVStages * kTile + 256;
+};
+
+enum : int {
+  DQ_OUTER = 0, DQ_KFULL = 1, DQ_KEMPTY = 5, DQ_VFULL = 9, DQ_VEMPTY = 13, DQ_SFULL = 17, DQ_SFREE = 18,
+  DQ_DPFULL = 19 /* + 2 */, DQ_DSREADY = 21, DQ_ACC = 22, DQ_DRAIN = 23
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                  const BwdParams p) {
+  using C = DqCfg<D>;
+  constexpr int KST = C::kKStages, VST = C::kVStages;
+  bool smem_ok;
+  const BwdSmem sm = bwd_smem<C::kUsed>(smem_ok);
+#define BAR(i) (sm.bar0 + 8u * static_cast<uint32_t>(i))
+  const uint32_t sQ = sm.base + C::kOffQ, sdO = sm.base + C::kOffdO;
+  const uint32_t sK = sm.base + C::kOffK, sV = sm.base + C::kOffV;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0 && smem_ok) {
+    mbar_init(BAR(DQ_OUTER), 1);
+    for (int s = 0; s < 4; ++s) {
+      mbar_init(BAR(DQ_KFULL + s), 1);
+      mbar_init(BAR(DQ_KEMPTY + s), 1);
+      mbar_init(BAR(DQ_VFULL + s), 1);
+      mbar_init(BAR(DQ_VEMPTY + s), 1);
+    }
+    mbar_init(BAR(DQ_SFULL), 1);
+    mbar_init(BAR(DQ_SFREE), 256);
+    mbar_init(BAR(DQ_DPFULL + 0), 1);
+    mbar_init(BAR(DQ_DPFULL + 1), 1);
+    mbar_init(BAR(DQ_DSREADY), 256);
+    mbar_init(BAR(DQ_ACC), 1);
+    mbar_init(BAR(DQ_DRAIN), 1);
+    fence_barrier_init();
+  }
+  uint32_t tmem;
+  if (!bwd_setup(sm, smem_ok, p, tmem)) return;
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  tmem = *sm.tmem_slot;
+
+  // work item: head major, query tile descending (the longest rows first)
+  const int nqt = (p.S + kBT - 1) / kBT;
+  const int bh = blockIdx.x / nqt;
+  const int i = nqt - 1 - (blockIdx.x - bh * nqt);
+  const int b = bh / p.H, h = bh - b * p.H;
+  const int bkv = b * p.H_kv + h / p.group;
+  const int nsteps = min(i * kBT + kBT - 1, p.S - 1) / kBT + 1;
+  const uint32_t tDQ = tmem, tS = tmem + 128, tDP = tmem + 256;
+
+  if (warp >= 8) {
+    if (warp == kBwdWarpLoadA) {
+      // ---------------- TMA: Q and dO once, then the K ring
+      if (lane == 0) {
+        const uint64_t pol_once = policy_evict_first();
+        const uint64_t pol_shared = policy_evict_last();
+        mbar_arrive_expect_tx(BAR(DQ_OUTER), 2 * C::kTile);
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_3d(sQ + c * (kBT * 128), &tmQ, BAR(DQ_OUTER), c * 64, i * kBT, bh, pol_once);
+          tma_load_3d(sdO + c * (kBT * 128), &tmdO, BAR(DQ_OUTER), c * 64, i * kBT, bh, pol_once);
+        }
+        int issued = 0;
+        for (int s = 0; s < nsteps; ++s) {
+          const int st = s % KST;
+          if (!mbar_wait(BAR(DQ_KEMPTY + st), ((s / KST) & 1) ^ 1, p.status, kDevTimeoutBwd)) break;
+          mbar_arrive_expect_tx(BAR(DQ_KFULL + st), C::kTile);
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_3d(sK + st * C::kTile + c * (kBT * 128), &tmK, BAR(DQ_KFULL + st), c * 64, s * kBT, bkv, pol_shared);
+          ++issued;
+        }
+        drain_wait(BAR(DQ_OUTER), 0, p.status);
+        for (int s = max(0, issued - KST); s < issued; ++s) drain_wait(BAR(DQ_KFULL + s % KST), (s / KST) & 1, p.status);
+      }
+      __syncwarp();
+    } else if (warp == kBwdWarpLoadB) {
+      // ---------------- TMA: the V ring
+      if (lane == 0) {
+        const uint64_t pol_shared = policy_evict_last();
+        int issued = 0;
+        for (int s = 0; s < nsteps; ++s) {
+          const int st = s % VST;
+          if (!mbar_wait(BAR(DQ_VEMPTY + st), ((s / VST) & 1) ^ 1, p.status, kDevTimeoutBwd)) break;
+          mbar_arrive_expect_tx(BAR(DQ_VFULL + st), C::kTile);
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_3d(sV + st * C::kTile + c * (kBT * 128), &tmV, BAR(DQ_VFULL + st), c * 64, s * kBT, bkv, pol_shared);
+          ++issued;
+        }
+        for (int s = max(0, issued - VST); s < issued; ++s) drain_wait(BAR(DQ_VFULL + s % VST), (s / VST) & 1, p.status);
+      }
+      __syncwarp();
+    } else if (warp == kBwdWarpMma) {
+      // ---------------- UMMA issuer
+      if (lane == 0) {
+        const uint64_t dQd = sdesc_sw128(sQ, 16, 1024), dOd = sdesc_sw128(sdO, 16, 1024);
+        const uint64_t dKk = sdesc_sw128(sK, 16, 1024), dVk = sdesc_sw128(sV, 16, 1024);
+        const uint64_t dKm = sdesc_sw128(sK, kBT * 128, 1024);
+        bool ok = mbar_wait(BAR(DQ_OUTER), 0, p.status, kDevTimeoutBwd) &&
+                  mbar_wait(BAR(DQ_KFULL + 0), 0, p.status, kDevTimeoutBwd) &&
+                  mbar_wait(BAR(DQ_VFULL + 0), 0, p.status, kDevTimeoutBwd);
+        if (ok) {
+          tc_fence_after();
+          umma_rows_rows<D, BF16>(tS, dQd, dKk);  // S(0) = Q K_0^T
+          umma_commit(BAR(DQ_SFULL));
+          umma_rows_rows<D, BF16>(tDP, dOd, dVk);  // dP(0) = dO V_0^T
+          umma_commit(BAR(DQ_DPFULL + 0));
+          umma_commit(BAR(DQ_VEMPTY + 0));
+        }
+        for (int s = 0; ok && s < nsteps; ++s) {
+          if (s + 1 < nsteps) {
+            const int k1 = (s + 1) % KST, v1 = (s + 1) % VST;
+            if (!(ok = mbar_wait(BAR(DQ_SFREE), s & 1, p.status, kDevTimeoutBwd))) break;
+            if (!(ok = mbar_wait(BAR(DQ_KFULL + k1), ((s + 1) / KST) & 1, p.status, kDevTimeoutBwd))) break;
+            tc_fence_after();
+            umma_rows_rows<D, BF16>(tS, dQd, desc_add(dKk, k1 * C::kTile));
+            umma_commit(BAR(DQ_SFULL));
+            if (!(ok = mbar_wait(BAR(DQ_VFULL + v1), ((s + 1) / VST) & 1, p.status, kDevTimeoutBwd))) break;
+            tc_fence_after();
+            umma_rows_rows<D, BF16>(tDP + 128 * ((s + 1) & 1), dOd, desc_add(dVk, v1 * C::kTile));
+            umma_commit(BAR(DQ_DPFULL + ((s + 1) & 1)));
+            umma_commit(BAR(DQ_VEMPTY + v1));
+          }
+          if (!(ok = mbar_wait(BAR(DQ_DSREADY), s & 1, p.status, kDevTimeoutBwd))) break;
+          tc_fence_after();
+          umma_tmem_tile<D, BF16>(tDQ, tDP + 128 * (s & 1), desc_add(dKm, (s % KST) * C::kTile), s > 0 ? 1u : 0u);
+          umma_commit(BAR(DQ_KEMPTY + s % KST));
+        }
+        if (ok) umma_commit(BAR(DQ_ACC));
+        umma_commit(BAR(DQ_DRAIN));
+        drain_wait(BAR(DQ_DRAIN), 0, p.status);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ---------------- compute warpgroups: warpgroup w owns columns [64 w, 64 w + 64)
+    const int w = warp / 4, wq = warp % 4;
+    const int row = wq * 32 + lane;
+    const int qrow = i * kBT + row;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const size_t ridx = static_cast<size_t>(bh) * p.S + qrow;
+    const float lse_r = qrow < p.S ? p.lse[ridx] : 0.f;
+    const float del_r = qrow < p.S ? p.delta[ridx] : 0.f;
+    float neg_lse[64];
+#pragma unroll
+    for (int c = 0; c < 64; ++c) neg_lse[c] = -lse_r;
+    bool ok = true;
+    for (int s = 0; s < nsteps; ++s) {
+      if (!(ok = mbar_wait(BAR(DQ_SFULL), s & 1, p.status, kDevTimeoutBwd))) break;
+      tc_fence_after();
+      uint32_t sv[2][32];
+      tmem_ld32(tS + lane_off + 64 * w, sv[0]);
+      tmem_ld32(tS + lane_off + 64 * w + 32, sv[1]);
+      tmem_ld_wait(sv[0]);
+      tmem_ld_wait(sv[1]);
+      tc_fence_before();
+      mbar_arrive(BAR(DQ_SFREE));
+      float pr[64];
+      exp2_row<32>(sv[0], neg_lse, p.scale_log2, pr);
+      exp2_row<32>(sv[1], neg_lse, p.scale_log2, pr + 32);
+      const int k0 = s * kBT + 64 * w;
+      if (k0 + 63 > i * kBT || k0 + 64 > p.S) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          if (k0 + c > qrow || k0 + c >= p.S) pr[c] = 0.f;
+      }
+      if (!(ok = mbar_wait(BAR(DQ_DPFULL + (s & 1)), (s >> 1) & 1, p.status, kDevTimeoutBwd))) break;
+      tc_fence_after();
+      const uint32_t tdp = tDP + 128 * (s & 1) + lane_off;
+      uint32_t dp[2][32];
+      tmem_ld32(tdp + 64 * w, dp[0]);
+      tmem_ld32(tdp + 64 * w + 32, dp[1]);
+      tmem_ld_wait(dp[0]);
+      tmem_ld_wait(dp[1]);
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int c2 = 0; c2 < 16; ++c2) {
+          const uint64_t d2 = fadd2(f2u(dp[h2][2 * c2], dp[h2][2 * c2 + 1]), f2(-del_r, -del_r));
+          const uint64_t ds = fmul2(f2(pr[32 * h2 + 2 * c2], pr[32 * h2 + 2 * c2 + 1]), d2);
+          pk[c2] = pack2<BF16>(f2lo(ds), f2hi(ds));
+        }
+        tmem_st16(tdp + 64 * w + 16 * h2, pk);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(BAR(DQ_DSREADY));
+    }
+    if (ok) ok = mbar_wait(BAR(DQ_ACC), 0, p.status, kDevTimeoutBwd);
+    if (ok) {
+      tc_fence_after();
+      uint8_t* orow = reinterpret_cast<uint8_t*>(p.dq) + ridx * (D * 2);
+#pragma unroll 1
+      for (int c = w * (D / 64); c < (w + 1) * (D / 64); ++c) {
+        uint32_t v[32];
+        tmem_ld32(tDQ + lane_off + c * 32, v);
+        tmem_ld_wait(v);
+        if (qrow < p.S) store_row_chunk<BF16>(orow + c * 64, v, p.sm_scale);
+      }
+    }
+  }
+#undef BAR
+  bwd_teardown(tmem);
 }
 
 // ---------------------------------------------------------------------------- dK / dV
+template <int D>
+struct DkdvCfg {
+  static constexpr int kTile = kBT * D * 2;
+  static constexpr int kPT = kBT * kBT * 2;  // P^T buffer: 128 keys x 128 queries, 16-bit
+  static constexpr int kStat = 2 * kBT * 4;   // LSE and delta slices of one query tile
+  static constexpr int kBudget = kSmemOptin - 768 - 256;
+  static constexpr int kStagesFit = (kBudget - 2 * kTile - kPT) / (2 * kTile + kStat);
+  static constexpr int kStages = kStagesFit > 4 ? 4 : kStagesFit;
+  static_assert(kStages >= 2, "need a double-buffered Q / dO ring");
+  static constexpr int kOffK = 0, kOffV = kTile, kOffPT = 2 * kTile;
+  static constexpr int kOffStages = kOffPT + kPT;  // stage st: Q, dO
+  static constexpr int kOffStats = kOffStages + kStages * 2 * kTile;
+  static constexpr int kUsed = kOffStats + kStages * kStat + 256;
+};
+
+enum : int {
+  KV_OUTER = 0, KV_SFULL = 1 /* + stage */, KV_SEMPTY = 5 /* + stage */, KV_STFULL = 9, KV_STFREE = 10,
+  KV_PREADY = 11, KV_PTFREE = 12, KV_DPFULL = 13, KV_DSREADY = 14, KV_ACC = 15, KV_DRAIN = 16
+};
+
 template <int D, bool BF16>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                     const BwdParams p) {
-  using C = BwdCfg<D>;
+  using C = DkdvCfg<D>;
   constexpr int ST = C::kStages;
-  constexpr uint32_t IDESC_SD = idesc_f16(BF16, kBO, kBI, false, false);
-  constexpr uint32_t IDESC_ACC = idesc_f16(BF16, kBO, D, false, true);
-  const BwdSmem sm = bwd_smem<C>();
-  auto bar = [&](int i) -> uint32_t { return smem_u32(sm.bars + i); };
-  const uint32_t sOA = sm.base + C::kOffOuterA, sOB = sm.base + C::kOffOuterB;
-  auto stage = [&](int st) -> uint32_t { return sm.base + C::kOffStages + st * C::kStageBytes; };
-
+  bool smem_ok;
+  const BwdSmem sm = bwd_smem<C::kUsed>(smem_ok);
+#define BAR(i) (sm.bar0 + 8u * static_cast<uint32_t>(i))
+  const uint32_t sK = sm.base + C::kOffK, sV = sm.base + C::kOffV, sPT = sm.base + C::kOffPT;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0 && smem_ok) {
+    mbar_init(BAR(KV_OUTER), 1);
+    for (int s = 0; s < 4; ++s) {
+      mbar_init(BAR(KV_SFULL + s), 1);
+      mbar_init(BAR(KV_SEMPTY + s), 1);
+    }
+    mbar_init(BAR(KV_STFULL), 1);
+    mbar_init(BAR(KV_STFREE), 256);
+    mbar_init(BAR(KV_PREADY), 256);
+    mbar_init(BAR(KV_PTFREE), 1);
+    mbar_init(BAR(KV_DPFULL), 1);
+    mbar_init(BAR(KV_DSREADY), 256);
+    mbar_init(BAR(KV_ACC), 1);
+    mbar_init(BAR(KV_DRAIN), 1);
+    fence_barrier_init();
+  }
   uint32_t tmem;
-  if (!bwd_setup<C>(sm, p, tmem)) return;
+  if (!bwd_setup(sm, smem_ok, p, tmem)) return;
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  tmem = *sm.tmem_slot;
 
   // work item: (b, kv head) major, key tile ascending (tile 0 sees every query: heaviest first)
-  const int nkt = (p.S + kBO - 1) / kBO;
+  const int nkt = (p.S + kBT - 1) / kBT;
   const int bkv = blockIdx.x / nkt;
   const int j = blockIdx.x - bkv * nkt;
   const int b = bkv / p.H_kv, g = bkv - b * p.H_kv;
-  const int nqi_total = p.S / kBI;
-  const int i_start = (j * kBO) / kBI;
-  const int nqi = nqi_total - i_start;
+  const int nqi = nkt - j;  // query tiles j .. nkt-1 see these keys
   const int nsteps = p.group * nqi;
+  const uint32_t tDV = tmem, tDK = tmem + 128, tST = tmem + 256, tDPT = tmem + 384;
 
-  if (warp == kBwdWarpProducer) {
-    if (lane == 0) {
-      const uint64_t pol_once = policy_evict_first();    // outer tile: read by this CTA only
-      const uint64_t pol_shared = policy_evict_last();   // inner tiles: read by many CTAs
-      mbar_arrive_expect_tx(bar(BB_OUTER), 2 * C::kOuterBytes);
-      for (int c = 0; c < C::kChunks; ++c) {
-        tma_load_3d(sOA + c * C::kOuterChunk, &tmK, bar(BB_OUTER), c * 64, j * kBO, bkv, pol_once);
-        tma_load_3d(sOB + c * C::kOuterChunk, &tmV, bar(BB_OUTER), c * 64, j * kBO, bkv, pol_once);
-      }
-      int issued = 0;
-      for (int s = 0; s < nsteps; ++s) {
-        const int st = s % ST;
-        if (!mbar_wait(bar(BB_SEMPTY + st), ((s / ST) & 1) ^ 1, p.status, kDevTimeoutBwd)) break;
-        const int hh = s / nqi, i = i_start + (s - hh * nqi);
-        const int bh = b * p.H + g * p.group + hh;
-        const uint32_t sb = stage(st);
-        mbar_arrive_expect_tx(bar(BB_SFULL + st), 2 * C::kInnerBytes + 2 * C::kStatBytes);
-        for (int c = 0; c < C::kChunks; ++c) {
-          tma_load_3d(sb + C::kStInA + c * C::kInnerChunk, &tmQ, bar(BB_SFULL + st), c * 64, i * kBI, bh, pol_shared);
-          tma_load_3d(sb + C::kStInB + c * C::kInnerChunk, &tmdO, bar(BB_SFULL + st), c * 64, i * kBI, bh, pol_shared);
+  if (warp >= 8) {
+    if (warp == kBwdWarpLoadA) {
+      // ---------------- TMA: K and V once, then Q / dO tiles with their LSE / delta slices
+      if (lane == 0) {
+        const uint64_t pol_once = policy_evict_first();
+        const uint64_t pol_shared = policy_evict_last();
+        mbar_arrive_expect_tx(BAR(KV_OUTER), 2 * C::kTile);
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_3d(sK + c * (kBT * 128), &tmK, BAR(KV_OUTER), c * 64, j * kBT, bkv, pol_once);
+          tma_load_3d(sV + c * (kBT * 128), &tmV, BAR(KV_OUTER), c * 64, j * kBT, bkv, pol_once);
         }
-        const size_t row0 = static_cast<size_t>(bh) * p.S + static_cast<size_t>(i) * kBI;
-        bulk_load(sb + C::kStLse, p.lse + row0, C::kStatBytes, bar(BB_SFULL + st));
-        bulk_load(sb + C::kStDelta, p.delta + row0, C::kStatBytes, bar(BB_SFULL + st));
-        ++issued;
+        int issued = 0;
+        for (int s = 0; s < nsteps; ++s) {
+          const int st = s % ST;
+          if (!mbar_wait(BAR(KV_SEMPTY + st), ((s / ST) & 1) ^ 1, p.status, kDevTimeoutBwd)) break;
+          const int hh = s / nqi, it = j + (s - hh * nqi);
+          const int bh = b * p.H + g * p.group + hh;
+          const uint32_t sQs = sm.base + C::kOffStages + st * 2 * C::kTile;
+          const uint32_t stat = sm.base + C::kOffStats + st * C::kStat;
+          const int rows = min(kBT, p.S - it * kBT);  // a multiple of 64 (S % 64 == 0)
+          mbar_arrive_expect_tx(BAR(KV_SFULL + st), 2 * C::kTile + 2 * rows * 4);
+          for (int c = 0; c < D / 64; ++c) {
+            tma_load_3d(sQs + c * (kBT * 128), &tmQ, BAR(KV_SFULL + st), c * 64, it * kBT, bh, pol_shared);
+            tma_load_3d(sQs + C::kTile + c * (kBT * 128), &tmdO, BAR(KV_SFULL + st), c * 64, it * kBT, bh, pol_shared);
+          }
+          const size_t row0 = static_cast<size_t>(bh) * p.S + static_cast<size_t>(it) * kBT;
+          bulk_load(stat, p.lse + row0, rows * 4, BAR(KV_SFULL + st));
+          bulk_load(stat + kBT * 4, p.delta + row0, rows * 4, BAR(KV_SFULL + st));
+          ++issued;
+        }
+        drain_wait(BAR(KV_OUTER), 0, p.status);
+        for (int s = max(0, issued - ST); s < issued; ++s) drain_wait(BAR(KV_SFULL + s % ST), (s / ST) & 1, p.status);
       }
-      drain_wait(bar(BB_OUTER), 0, p.status);
-      for (int s = max(0, issued - ST); s < issued; ++s)
-        drain_wait(bar(BB_SFULL + s % ST), (s / ST) & 1, p.status);
-    }
-    __syncwarp();
-  } else if (warp == kBwdWarpMma) {
-    if (lane == 0) {
-      // descriptors: outer K / V (K-major), inner Q / dO of stage 0 as K-major (S^T, dP^T) and
-      // as MN-major B operands (dK, dV); stage st adds st * kStageBytes
-      const uint64_t dK_ = sdesc_sw128(sOA, 16, 1024), dV_ = sdesc_sw128(sOB, 16, 1024);
-      const uint64_t dQk = sdesc_sw128(stage(0) + C::kStInA, 16, 1024);
-      const uint64_t dOk = sdesc_sw128(stage(0) + C::kStInB, 16, 1024);
-      const uint64_t dQm = sdesc_sw128(stage(0) + C::kStInA, C::kInnerChunk, 1024);
-      const uint64_t dOm = sdesc_sw128(stage(0) + C::kStInB, C::kInnerChunk, 1024);
-      bool ok = mbar_wait(bar(BB_OUTER), 0, p.status, kDevTimeoutBwd) &&
-                mbar_wait(bar(BB_SFULL + 0), 0, p.status, kDevTimeoutBwd);
-      if (ok) {
-        tc_fence_after();
-        umma_outer_inner<D, C>(tmem + 256, dK_, dQk, IDESC_SD);       // S^T = K Q^T
-        umma_outer_inner<D, C>(tmem + 256 + 64, dV_, dOk, IDESC_SD);  // dP^T = V dO^T
-        umma_commit(bar(BB_MFULL + 0));
-      }
-      for (int s = 0; ok && s < nsteps; ++s) {
-        const int st = s % ST, bf = s & 1;
-        if (s + 1 < nsteps) {
-          const int st1 = (s + 1) % ST, bf1 = (s + 1) & 1;
-          if (!(ok = mbar_wait(bar(BB_SFULL + st1), ((s + 1) / ST) & 1, p.status, kDevTimeoutBwd))) break;
+      __syncwarp();
+    } else if (warp == kBwdWarpMma) {
+      // ---------------- UMMA issuer
+      if (lane == 0) {
+        const uint64_t dKd = sdesc_sw128(sK, 16, 1024), dVd = sdesc_sw128(sV, 16, 1024);
+        const uint64_t dPTd = sdesc_sw128(sPT, 16, 1024);
+        const uint32_t s0 = sm.base + C::kOffStages;
+        const uint64_t dQk = sdesc_sw128(s0, 16, 1024), dOk = sdesc_sw128(s0 + C::kTile, 16, 1024);
+        const uint64_t dQm = sdesc_sw128(s0, kBT * 128, 1024), dOm = sdesc_sw128(s0 + C::kTile, kBT * 128, 1024);
+        constexpr uint32_t kStageStep = 2 * C::kTile;
+        bool ok = mbar_wait(BAR(KV_OUTER), 0, p.status, kDevTimeoutBwd) &&
+                  mbar_wait(BAR(KV_SFULL + 0), 0, p.status, kDevTimeoutBwd);
+        if (ok) {
           tc_fence_after();
-          const uint64_t so = static_cast<uint64_t>((st1 * C::kStageBytes) >> 4);
-          umma_outer_inner<D, C>(tmem + 256 + 128 * bf1, dK_, dQk + so, IDESC_SD);
-          umma_outer_inner<D, C>(tmem + 256 + 128 * bf1 + 64, dV_, dOk + so, IDESC_SD);
-          umma_commit(bar(BB_MFULL + bf1));
+          umma_rows_rows<D, BF16>(tST, dKd, dQk);  // S^T(0) = K Q_0^T
+          umma_commit(BAR(KV_STFULL));
+          umma_rows_rows<D, BF16>(tDPT, dVd, dOk);  // dP^T(0) = V dO_0^T
+          umma_commit(BAR(KV_DPFULL));
         }
-        if (!(ok = mbar_wait(bar(BB_PFULL + bf), (s >> 1) & 1, p.status, kDevTimeoutBwd))) break;
-        tc_fence_after();
-        const uint64_t so = static_cast<uint64_t>((st * C::kStageBytes) >> 4);
-        const uint32_t acc = s > 0 ? 1u : 0u;
-        umma_tmem_inner<D, C>(tmem + 0, tmem + 256 + 128 * bf, dOm + so, IDESC_ACC, acc);         // dV += P^T dO
-        umma_tmem_inner<D, C>(tmem + 128, tmem + 256 + 128 * bf + 64, dQm + so, IDESC_ACC, acc);  // dK += dS^T Q
-        umma_commit(bar(BB_SEMPTY + st));
+        for (int s = 0; ok && s < nsteps; ++s) {
+          const int st = s % ST;
+          const uint32_t so = st * kStageStep;
+          if (s + 1 < nsteps) {
+            const uint32_t so1 = ((s + 1) % ST) * kStageStep;
+            if (!(ok = mbar_wait(BAR(KV_STFREE), s & 1, p.status, kDevTimeoutBwd))) break;
+            if (!(ok = mbar_wait(BAR(KV_SFULL + (s + 1) % ST), ((s + 1) / ST) & 1, p.status, kDevTimeoutBwd))) break;
+            tc_fence_after();
+            umma_rows_rows<D, BF16>(tST, dKd, desc_add(dQk, so1));
+            umma_commit(BAR(KV_STFULL));
+          }
+          if (!(ok = mbar_wait(BAR(KV_PREADY), s & 1, p.status, kDevTimeoutBwd))) break;
+          tc_fence_after();
+          umma_smem_tile<D, BF16>(tDV, dPTd, desc_add(dOm, so), s > 0 ? 1u : 0u);  // dV += P^T dO
+          umma_commit(BAR(KV_PTFREE));
+          if (!(ok = mbar_wait(BAR(KV_DSREADY), s & 1, p.status, kDevTimeoutBwd))) break;
+          tc_fence_after();
+          umma_tmem_tile<D, BF16>(tDK, tDPT, desc_add(dQm, so), s > 0 ? 1u : 0u);  // dK += dS^T Q
+          umma_commit(BAR(KV_SEMPTY + st));
+          if (s + 1 < nsteps) {
+            umma_rows_rows<D, BF16>(tDPT, dVd, desc_add(dOk, ((s + 1) % ST) * kStageStep));
+            umma_commit(BAR(KV_DPFULL));
+          }
+        }
+        if (ok) umma_commit(BAR(KV_ACC));
+        umma_commit(BAR(KV_DRAIN));
+        drain_wait(BAR(KV_DRAIN), 0, p.status);
       }
-      if (ok) umma_commit(bar(BB_ACC));
-      umma_commit(bar(BB_DRAIN));
-      drain_wait(bar(BB_DRAIN), 0, p.status);
+      __syncwarp();
     }
-    __syncwarp();
-  } else if (warp < 8) {
-    const int w = warp / 4;  // compute warpgroup: steps s with s % 2 == w
-    const int wq = warp % 4;
+  } else {
+    // ---------------- compute warpgroups: warpgroup w owns query columns [64 w, 64 w + 64)
+    const int w = warp / 4, wq = warp % 4;
     const int row = wq * 32 + lane;
-    const int key = j * kBO + row;
+    const int key = j * kBT + row;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-    const uint32_t tS = tmem + 256 + 128 * w + lane_off;
-    const uint32_t tP = tS + 64;
     const float scale = p.scale_log2;
+    uint8_t* const pt_row = sm.ptr + C::kOffPT + w * (kBT * 128) + row * 128;
     bool ok = true;
-    for (int s = w; s < nsteps; s += 2) {
-      if (!(ok = mbar_wait(bar(BB_MFULL + w), (s >> 1) & 1, p.status, kDevTimeoutBwd))) break;
-      tc_fence_after();
+    for (int s = 0; s < nsteps; ++s) {
       const int st = s % ST;
-      const int hh = s / nqi, i = i_start + (s - hh * nqi);
-      uint32_t sv[2][32], dp[2][32];
-      tmem_ld32(tS, sv[0]);
-      tmem_ld32(tS + 32, sv[1]);
-      tmem_ld32(tP, dp[0]);
-      tmem_ld32(tP + 32, dp[1]);
+      const int hh = s / nqi, it = j + (s - hh * nqi);
+      if (!(ok = mbar_wait(BAR(KV_STFULL), s & 1, p.status, kDevTimeoutBwd))) break;
+      tc_fence_after();
+      uint32_t sv[2][32];
+      tmem_ld32(tST + lane_off + 64 * w, sv[0]);
+      tmem_ld32(tST + lane_off + 64 * w + 32, sv[1]);
       tmem_ld_wait(sv[0]);
       tmem_ld_wait(sv[1]);
+      tc_fence_before();
+      mbar_arrive(BAR(KV_STFREE));
+      const float* lse = reinterpret_cast<const float*>(sm.ptr + C::kOffStats + st * C::kStat) + 64 * w;
+      const float* del = lse + kBT;
+      float neg_lse[64];
+#pragma unroll
+      for (int c = 0; c < 64; c += 4) {
+        const float4 l4 = *reinterpret_cast<const float4*>(lse + c);
+        neg_lse[c] = -l4.x;
+        neg_lse[c + 1] = -l4.y;
+        neg_lse[c + 2] = -l4.z;
+        neg_lse[c + 3] = -l4.w;
+      }
+      float pr[64];
+      exp2_row<32>(sv[0], neg_lse, scale, pr);
+      exp2_row<32>(sv[1], neg_lse + 32, scale, pr + 32);
+      const int q0 = it * kBT + 64 * w;
+      if (key > q0 || q0 + 64 > p.S) {  // some query of these 64 precedes the key, or lies past S
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          if (key > q0 + c || q0 + c >= p.S) pr[c] = 0.f;
+      }
+      // P^T -> shared memory (row = key, 128-byte swizzle), once dV of the previous step is done
+      if (s > 0 && !(ok = mbar_wait(BAR(KV_PTFREE), (s - 1) & 1, p.status, kDevTimeoutBwd))) break;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const uint4 v = make_uint4(pack2<BF16>(pr[8 * u], pr[8 * u + 1]), pack2<BF16>(pr[8 * u + 2], pr[8 * u + 3]),
+                                   pack2<BF16>(pr[8 * u + 4], pr[8 * u + 5]), pack2<BF16>(pr[8 * u + 6], pr[8 * u + 7]));
+        *reinterpret_cast<uint4*>(pt_row + ((u ^ (row & 7)) << 4)) = v;
+      }
+      fence_async_shared();
+      mbar_arrive(BAR(KV_PREADY));
+      // dS^T = P^T (dP^T - delta) -> TMEM over dP^T
+      if (!(ok = mbar_wait(BAR(KV_DPFULL), s & 1, p.status, kDevTimeoutBwd))) break;
+      tc_fence_after();
+      uint32_t dp[2][32];
+      tmem_ld32(tDPT + lane_off + 64 * w, dp[0]);
+      tmem_ld32(tDPT + lane_off + 64 * w + 32, dp[1]);
       tmem_ld_wait(dp[0]);
       tmem_ld_wait(dp[1]);
-      const float4* lse4 = reinterpret_cast<const float4*>(sm.ptr + C::kOffStages + st * C::kStageBytes + C::kStLse);
-      const float4* del4 = reinterpret_cast<const float4*>(sm.ptr + C::kOffStages + st * C::kStageBytes + C::kStDelta);
-      const int q0 = i * kBI;
-      const bool need_mask = q0 < j * kBO + kBO;
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
-        uint32_t pk[16], dk[16];
+        uint32_t pk[16];
 #pragma unroll
         for (int c4 = 0; c4 < 8; ++c4) {
-          const float4 l4 = lse4[h2 * 8 + c4];
-          const float4 d4 = del4[h2 * 8 + c4];
-          const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-          const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
-          float pr[4], ds[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int c = c4 * 4 + e;
-            float pv = ex2_approx(fmaf(__uint_as_float(sv[h2][c]), scale, -lv[e]));
-            if (need_mask && key > q0 + h2 * 32 + c) pv = 0.f;
-            pr[e] = pv;
-            ds[e] = pv * (__uint_as_float(dp[h2][c]) - dv[e]);
-          }
-          pk[2 * c4] = pack2<BF16>(pr[0], pr[1]);
-          pk[2 * c4 + 1] = pack2<BF16>(pr[2], pr[3]);
-          dk[2 * c4] = pack2<BF16>(ds[0], ds[1]);
-          dk[2 * c4 + 1] = pack2<BF16>(ds[2], ds[3]);
+          const float4 d4 = *reinterpret_cast<const float4*>(del + 32 * h2 + 4 * c4);
+          const int c = 32 * h2 + 4 * c4;
+          const uint64_t a = fmul2(f2(pr[c], pr[c + 1]),
+                                   fadd2(f2u(dp[h2][4 * c4], dp[h2][4 * c4 + 1]), f2(-d4.x, -d4.y)));
+          const uint64_t bb = fmul2(f2(pr[c + 2], pr[c + 3]),
+                                    fadd2(f2u(dp[h2][4 * c4 + 2], dp[h2][4 * c4 + 3]), f2(-d4.z, -d4.w)));
+          pk[2 * c4] = pack2<BF16>(f2lo(a), f2hi(a));
+          pk[2 * c4 + 1] = pack2<BF16>(f2lo(bb), f2hi(bb));
         }
-        tmem_st16(tS + h2 * 16, pk);
-        tmem_st16(tP + h2 * 16, dk);
+        tmem_st16(tDPT + lane_off + 64 * w + 16 * h2, pk);
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(bar(BB_PFULL + w));
+      mbar_arrive(BAR(KV_DSREADY));
     }
-    if (ok) ok = mbar_wait(bar(BB_ACC), 0, p.status, kDevTimeoutBwd);
+    if (ok) ok = mbar_wait(BAR(KV_ACC), 0, p.status, kDevTimeoutBwd);
     if (ok) {
       tc_fence_after();
       // warpgroup 0 writes dV rows, warpgroup 1 writes dK rows (scaled by 1/sqrt(D))
       void* out = (w == 0) ? p.dv : p.dk;
       const float osc = (w == 0) ? 1.0f : p.sm_scale;
-      const uint32_t tacc = tmem + (w == 0 ? 0 : 128) + lane_off;
+      const uint32_t tacc = (w == 0 ? tDV : tDK) + lane_off;
       uint8_t* orow = reinterpret_cast<uint8_t*>(out) + (static_cast<size_t>(bkv) * p.S + key) * (D * 2);
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
@@ -381,186 +654,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
   }
-  bwd_teardown(tmem);
-}
-
-// ---------------------------------------------------------------------------- dQ
-template <int D, bool BF16>
-__global__ void __launch_bounds__(kBwdThreads, 1)
-    bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                  const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
-                  const BwdParams p) {
-  using C = BwdCfg<D>;
-  constexpr int ST = C::kStages;
-  constexpr uint32_t IDESC_SD = idesc_f16(BF16, kBO, kBI, false, false);
-  constexpr uint32_t IDESC_ACC = idesc_f16(BF16, kBO, D, false, true);
-  const BwdSmem sm = bwd_smem<C>();
-  auto bar = [&](int i) -> uint32_t { return smem_u32(sm.bars + i); };
-  const uint32_t sOA = sm.base + C::kOffOuterA, sOB = sm.base + C::kOffOuterB;
-  auto stage = [&](int st) -> uint32_t { return sm.base + C::kOffStages + st * C::kStageBytes; };
-
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  uint32_t tmem;
-  if (!bwd_setup<C>(sm, p, tmem)) return;
-
-  // work item: head major, query tile descending (the longest rows first)
-  const int nqt = (p.S + kBO - 1) / kBO;
-  const int bh = blockIdx.x / nqt;
-  const int i = nqt - 1 - (blockIdx.x - bh * nqt);
-  const int b = bh / p.H, h = bh - b * p.H;
-  const int bkv = b * p.H_kv + h / p.group;
-  const int last_row = min(i * kBO + kBO - 1, p.S - 1);
-  const int nsteps = last_row / kBI + 1;
-
-  if (warp == kBwdWarpProducer) {
-    if (lane == 0) {
-      const uint64_t pol_once = policy_evict_first();    // outer tile: read by this CTA only
-      const uint64_t pol_shared = policy_evict_last();   // inner tiles: read by many CTAs
-      mbar_arrive_expect_tx(bar(BB_OUTER), 2 * C::kOuterBytes);
-      for (int c = 0; c < C::kChunks; ++c) {
-        tma_load_3d(sOA + c * C::kOuterChunk, &tmQ, bar(BB_OUTER), c * 64, i * kBO, bh, pol_once);
-        tma_load_3d(sOB + c * C::kOuterChunk, &tmdO, bar(BB_OUTER), c * 64, i * kBO, bh, pol_once);
-      }
-      int issued = 0;
-      for (int s = 0; s < nsteps; ++s) {
-        const int st = s % ST;
-        if (!mbar_wait(bar(BB_SEMPTY + st), ((s / ST) & 1) ^ 1, p.status, kDevTimeoutBwd)) break;
-        const uint32_t sb = stage(st);
-        mbar_arrive_expect_tx(bar(BB_SFULL + st), 2 * C::kInnerBytes);
-        for (int c = 0; c < C::kChunks; ++c) {
-          tma_load_3d(sb + C::kStInA + c * C::kInnerChunk, &tmK, bar(BB_SFULL + st), c * 64, s * kBI, bkv, pol_shared);
-          tma_load_3d(sb + C::kStInB + c * C::kInnerChunk, &tmV, bar(BB_SFULL + st), c * 64, s * kBI, bkv, pol_shared);
-        }
-        ++issued;
-      }
-      drain_wait(bar(BB_OUTER), 0, p.status);
-      for (int s = max(0, issued - ST); s < issued; ++s)
-        drain_wait(bar(BB_SFULL + s % ST), (s / ST) & 1, p.status);
-    }
-    __syncwarp();
-  } else if (warp == kBwdWarpMma) {
-    if (lane == 0) {
-      const uint64_t dQ_ = sdesc_sw128(sOA, 16, 1024), dO_ = sdesc_sw128(sOB, 16, 1024);
-      const uint64_t dKk = sdesc_sw128(stage(0) + C::kStInA, 16, 1024);
-      const uint64_t dVk = sdesc_sw128(stage(0) + C::kStInB, 16, 1024);
-      const uint64_t dKm = sdesc_sw128(stage(0) + C::kStInA, C::kInnerChunk, 1024);
-      bool ok = mbar_wait(bar(BB_OUTER), 0, p.status, kDevTimeoutBwd) &&
-                mbar_wait(bar(BB_SFULL + 0), 0, p.status, kDevTimeoutBwd);
-      if (ok) {
-        tc_fence_after();
-        umma_outer_inner<D, C>(tmem + 256, dQ_, dKk, IDESC_SD);       // S = Q K^T
-        umma_outer_inner<D, C>(tmem + 256 + 64, dO_, dVk, IDESC_SD);  // dP = dO V^T
-        umma_commit(bar(BB_MFULL + 0));
-      }
-      for (int s = 0; ok && s < nsteps; ++s) {
-        const int st = s % ST, bf = s & 1;
-        if (s + 1 < nsteps) {
-          const int st1 = (s + 1) % ST, bf1 = (s + 1) & 1;
-          if (!(ok = mbar_wait(bar(BB_SFULL + st1), ((s + 1) / ST) & 1, p.status, kDevTimeoutBwd))) break;
-          tc_fence_after();
-          const uint64_t so = static_cast<uint64_t>((st1 * C::kStageBytes) >> 4);
-          umma_outer_inner<D, C>(tmem + 256 + 128 * bf1, dQ_, dKk + so, IDESC_SD);
-          umma_outer_inner<D, C>(tmem + 256 + 128 * bf1 + 64, dO_, dVk + so, IDESC_SD);
-          umma_commit(bar(BB_MFULL + bf1));
-        }
-        if (!(ok = mbar_wait(bar(BB_PFULL + bf), (s >> 1) & 1, p.status, kDevTimeoutBwd))) break;
-        tc_fence_after();
-        const uint64_t so = static_cast<uint64_t>((st * C::kStageBytes) >> 4);
-        umma_tmem_inner<D, C>(tmem + 0, tmem + 256 + 128 * bf + 64, dKm + so, IDESC_ACC, s > 0 ? 1u : 0u);  // dQ += dS K
-        umma_commit(bar(BB_SEMPTY + st));
-      }
-      if (ok) umma_commit(bar(BB_ACC));
-      umma_commit(bar(BB_DRAIN));
-      drain_wait(bar(BB_DRAIN), 0, p.status);
-    }
-    __syncwarp();
-  } else if (warp < 8) {
-    const int w = warp / 4;
-    const int wq = warp % 4;
-    const int row = wq * 32 + lane;
-    const int qrow = i * kBO + row;
-    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-    const uint32_t tS = tmem + 256 + 128 * w + lane_off;
-    const uint32_t tP = tS + 64;
-    const float scale = p.scale_log2;
-    const size_t ridx = static_cast<size_t>(bh) * p.S + qrow;
-    const float lse_r = qrow < p.S ? p.lse[ridx] : 0.f;
-    const float del_r = qrow < p.S ? p.delta[ridx] : 0.f;
-    bool ok = true;
-    for (int s = w; s < nsteps; s += 2) {
-      if (!(ok = mbar_wait(bar(BB_MFULL + w), (s >> 1) & 1, p.status, kDevTimeoutBwd))) break;
-      tc_fence_after();
-      uint32_t sv[2][32], dp[2][32];
-      tmem_ld32(tS, sv[0]);
-      tmem_ld32(tS + 32, sv[1]);
-      tmem_ld32(tP, dp[0]);
-      tmem_ld32(tP + 32, dp[1]);
-      tmem_ld_wait(sv[0]);
-      tmem_ld_wait(sv[1]);
-      tmem_ld_wait(dp[0]);
-      tmem_ld_wait(dp[1]);
-      const int k0 = s * kBI;
-      const bool need_mask = k0 + kBI - 1 > i * kBO;
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        uint32_t dk[16];
-#pragma unroll
-        for (int c2 = 0; c2 < 16; ++c2) {
-          float ds2[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int c = 2 * c2 + e;
-            float pv = ex2_approx(fmaf(__uint_as_float(sv[h2][c]), scale, -lse_r));
-            if (need_mask && k0 + h2 * 32 + c > qrow) pv = 0.f;
-            ds2[e] = pv * (__uint_as_float(dp[h2][c]) - del_r);
-          }
-          dk[c2] = pack2<BF16>(ds2[0], ds2[1]);
-        }
-        tmem_st16(tP + h2 * 16, dk);
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(bar(BB_PFULL + w));
-    }
-    if (w == 0) {
-      if (ok) ok = mbar_wait(bar(BB_ACC), 0, p.status, kDevTimeoutBwd);
-      if (ok) {
-        tc_fence_after();
-        uint8_t* orow = reinterpret_cast<uint8_t*>(p.dq) + ridx * (D * 2);
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld32(tmem + lane_off + c * 32, v);
-          tmem_ld_wait(v);
-          if (qrow < p.S) store_row_chunk<BF16>(orow + c * 64, v, p.sm_scale);
-        }
-      }
-    }
-  }
+#undef BAR
   bwd_teardown(tmem);
 }
 
 template <int D, bool BF16>
 cudaError_t launch_dkdv_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
                           const CUtensorMap& tmdO, const BwdParams& p, cudaStream_t stream) {
-  using C = BwdCfg<D>;
   auto kern = bwd_dkdv_kernel<D, BF16>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemOptin);
   if (e != cudaSuccess) return e;
-  const int nkt = (p.S + kBO - 1) / kBO;
-  kern<<<p.B * p.H_kv * nkt, kBwdThreads, C::kSmemBytes, stream>>>(tmQ, tmK, tmV, tmdO, p);
+  const int nkt = (p.S + kBT - 1) / kBT;
+  kern<<<p.B * p.H_kv * nkt, kBwdThreads, kSmemOptin, stream>>>(tmQ, tmK, tmV, tmdO, p);
   return cudaGetLastError();
 }
 
 template <int D, bool BF16>
 cudaError_t launch_dq_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
                         const CUtensorMap& tmdO, const BwdParams& p, cudaStream_t stream) {
-  using C = BwdCfg<D>;
   auto kern = bwd_dq_kernel<D, BF16>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemOptin);
   if (e != cudaSuccess) return e;
-  const int nqt = (p.S + kBO - 1) / kBO;
-  kern<<<p.B * p.H * nqt, kBwdThreads, C::kSmemBytes, stream>>>(tmQ, tmK, tmV, tmdO, p);
+  const int nqt = (p.S + kBT - 1) / kBT;
+  kern<<<p.B * p.H * nqt, kBwdThreads, kSmemOptin, stream>>>(tmQ, tmK, tmV, tmdO, p);
   return cudaGetLastError();
 }
 

@@ -117,6 +117,27 @@ __device__ __forceinline__ Work decode_work(const FwdParams& p, int item) {
   return w;
 }
 
+// P = 2^(S * scale - m) for 32 columns of one row: packed f32x2 math; on unmasked tiles the pairs
+// in kPolyPairs (6 of 16) use the FMA-pipe polynomial, the rest the MUFU ex2, which balances the
+// two pipes.  Masked tiles use MUFU only, so masked entries (-inf) give exactly 0.
+constexpr uint32_t kPolyPairs = 0x5252u;  // pairs 1, 4, 6, 9, 12, 14
+
+template <bool kPoly, bool BF16>
+__device__ __forceinline__ void softmax_chunk(const uint32_t (&r)[32], uint64_t scale2, uint64_t negm2,
+                                              uint64_t (&sum2)[4], uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint64_t x2 = ffma2(f2u(r[2 * i], r[2 * i + 1]), scale2, negm2);
+    uint64_t p2;
+    if (kPoly && ((kPolyPairs >> i) & 1u))
+      p2 = exp2_poly2(f2lo(x2), f2hi(x2));
+    else
+      p2 = f2(ex2_approx(f2lo(x2)), ex2_approx(f2hi(x2)));
+    sum2[i & 3] = fadd2(sum2[i & 3], p2);
+    pk[i] = pack2<BF16>(f2lo(p2), f2hi(p2));
+  }
+}
+
 // S = Q K^T for one 128-row query tile: D/16 UMMAs, descriptors advanced by constant offsets.
 template <int D, int BN, bool BF16>
 __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint64_t q_desc, uint64_t k_desc) {
@@ -199,6 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  if (warp >= 8) {
   if (warp == kWarpProducerK) {
     // ------------------------------------------------------------ TMA: Q once, then the K ring
     if (lane == 0) {
@@ -313,7 +335,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       drain_wait(BAR(BAR_DRAIN), 0, p.status);
     }
     __syncwarp();
-  } else if (warp < 8) {
+  }
+  } else {
     // ------------------------------------------------------------ softmax / epilogue
     const int t = warp / 4;
     if (t < w.ntiles) {
@@ -339,7 +362,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c) tmem_ld_wait(r[c]);
         const int kbase = j * BN;
-        if (kbase + BN - 1 > tile.qt * kBM || kbase + BN > p.S) {
+        const bool masked = kbase + BN - 1 > tile.qt * kBM || kbase + BN > p.S;
+        if (masked) {
 #pragma unroll
           for (int c = 0; c < BN / 32; ++c)
 #pragma unroll
@@ -362,24 +386,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool upd = mt > m_used + kRescaleThreshold;
         const float m_new = upd ? mt : m_used;
         const float alpha = ex2_approx(m_used - m_new);
-        const float neg_m = -m_new;
-        float sum8[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) sum8[u] = 0.f;
+        const uint64_t scale2 = f2(scale, scale);
+        const uint64_t negm2 = f2(-m_new, -m_new);
+        uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float p0 = ex2_approx(fmaf(__uint_as_float(r[c][2 * i]), scale, neg_m));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(r[c][2 * i + 1]), scale, neg_m));
-            sum8[(2 * i) % 8] += p0;
-            sum8[(2 * i + 1) % 8] += p1;
-            pk[i] = pack2<BF16>(p0, p1);
-          }
+          if (masked)
+            softmax_chunk<false, BF16>(r[c], scale2, negm2, sum2, pk);
+          else
+            softmax_chunk<true, BF16>(r[c], scale2, negm2, sum2, pk);
           tmem_st16(tS + c * 16, pk);
         }
-        const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+        const uint64_t s01 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
+        const float sum = f2lo(s01) + f2hi(s01);
         l = l * alpha + sum;
         m_used = m_new;
         // Rescale the running O of this warp's rows if any row's max moved (P V of tile j-1 is

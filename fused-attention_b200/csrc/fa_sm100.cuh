@@ -35,6 +35,7 @@ enum DeviceError : int {
   kDevTimeoutO = 106,       // epilogue waiting for the last P V
   kDevTimeoutDrain = 107,   // teardown waiting for in-flight copies / MMAs
   kDevTimeoutBwd = 108,     // backward pipeline wait
+  kDevSmemLayout = 109,     // dynamic shared memory start leaves too little alignment slack
   kDevAborted = 199,        // another CTA already failed; this one stopped early
 };
 
@@ -329,6 +330,64 @@ __device__ __forceinline__ float lg2_approx(float x) {
   float y;
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// ---- packed fp32 pairs (sm_100 f32x2 instructions: one issue slot for two lanes of math)
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ uint64_t f2u(uint32_t lo, uint32_t hi) {
+  return (static_cast<uint64_t>(hi) << 32) | lo;
+}
+__device__ __forceinline__ float f2lo(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float f2hi(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair on the FMA pipe (relieves the MUFU pipe, which runs ex2 at 16 per clock per
+// SM).  x = n + f with n = rint(x) (via the 1.5 * 2^23 rounding constant) and f in [-1/2, 1/2];
+// 2^f ~ c0 + c1 f + c2 f^2 + c3 f^3, a minimax fit of the relative error over [-1/2, 1/2]
+// (Remez exchange; fused-attention_b200/csrc/fit_exp2_poly.py regenerates the coefficients):
+// max relative error 7.5e-5, below half an ulp of bfloat16 and ~0.3 ulp of float16.  2^n is
+// applied by adding n to the exponent field: the low 9 bits of the rounding sum hold n in two's
+// complement, so (bits(t) << 23) == n << 23.  x is clamped to >= -126 so the exponent stays >= 0;
+// results below ~2^-126 are tiny denormals instead of 0 (irrelevant for a softmax numerator).
+__device__ __forceinline__ uint64_t exp2_poly2(float x0, float x1) {
+  const uint64_t kRound = f2(12582912.0f, 12582912.0f);
+  const uint64_t kNegRound = f2(-12582912.0f, -12582912.0f);
+  const uint64_t kNegOne = f2(-1.0f, -1.0f);
+  const uint64_t c0 = f2(9.999280572e-01f, 9.999280572e-01f);
+  const uint64_t c1 = f2(6.932609677e-01f, 6.932609677e-01f);
+  const uint64_t c2 = f2(2.426111251e-01f, 2.426111251e-01f);
+  const uint64_t c3 = f2(5.517166853e-02f, 5.517166853e-02f);
+  const uint64_t x = f2(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+  const uint64_t t = fadd2(x, kRound);       // rint(x) in the low mantissa bits
+  const uint64_t n = fadd2(t, kNegRound);    // rint(x) as a float
+  const uint64_t fr = ffma2(n, kNegOne, x);  // x - rint(x)
+  uint64_t p = ffma2(c3, fr, c2);
+  p = ffma2(p, fr, c1);
+  p = ffma2(p, fr, c0);
+  const uint32_t lo = static_cast<uint32_t>(p) + (static_cast<uint32_t>(t) << 23);
+  const uint32_t hi = static_cast<uint32_t>(p >> 32) + (static_cast<uint32_t>(t >> 32) << 23);
+  return f2u(lo, hi);
 }
 
 // Pack two fp32 values into one 32-bit word of 16-bit floats (lo = first / lower k index).
