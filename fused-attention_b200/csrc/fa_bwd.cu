@@ -352,7 +352,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int c = 0; c < 64; ++c) neg_lse[c] = -lse_r;
     bool ok = true;
     for (int s = 0; s < nsteps; ++s) {
-      if (!(ok = mbar_wait(BAR(DQ_SFULL), s & 1, p.status, kDevTimeoutBwd))) break;
+      if (!(ok = warp_all(mbar_wait(BAR(DQ_SFULL), s & 1, p.status, kDevTimeoutBwd)))) break;
       tc_fence_after();
       uint32_t sv[2][32];
       tmem_ld32(tS + lane_off + 64 * w, sv[0]);
@@ -370,7 +370,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int c = 0; c < 64; ++c)
           if (k0 + c > qrow || k0 + c >= p.S) pr[c] = 0.f;
       }
-      if (!(ok = mbar_wait(BAR(DQ_DPFULL + (s & 1)), (s >> 1) & 1, p.status, kDevTimeoutBwd))) break;
+      if (!(ok = warp_all(mbar_wait(BAR(DQ_DPFULL + (s & 1)), (s >> 1) & 1, p.status, kDevTimeoutBwd)))) break;
       tc_fence_after();
       const uint32_t tdp = tDP + 128 * (s & 1) + lane_off;
       uint32_t dp[2][32];
@@ -394,6 +394,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_arrive(BAR(DQ_DSREADY));
     }
     if (ok) ok = mbar_wait(BAR(DQ_ACC), 0, p.status, kDevTimeoutBwd);
+    ok = warp_all(ok);
     if (ok) {
       tc_fence_after();
       uint8_t* orow = reinterpret_cast<uint8_t*>(p.dq) + ridx * (D * 2);
@@ -570,7 +571,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int s = 0; s < nsteps; ++s) {
       const int st = s % ST;
       const int hh = s / nqi, it = j + (s - hh * nqi);
-      if (!(ok = mbar_wait(BAR(KV_STFULL), s & 1, p.status, kDevTimeoutBwd))) break;
+      if (!(ok = warp_all(mbar_wait(BAR(KV_STFULL), s & 1, p.status, kDevTimeoutBwd)))) break;
       tc_fence_after();
       uint32_t sv[2][32];
       tmem_ld32(tST + lane_off + 64 * w, sv[0]);
@@ -600,7 +601,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (key > q0 + c || q0 + c >= p.S) pr[c] = 0.f;
       }
       // P^T -> shared memory (row = key, 128-byte swizzle), once dV of the previous step is done
-      if (s > 0 && !(ok = mbar_wait(BAR(KV_PTFREE), (s - 1) & 1, p.status, kDevTimeoutBwd))) break;
+      if (s > 0 && !(ok = warp_all(mbar_wait(BAR(KV_PTFREE), (s - 1) & 1, p.status, kDevTimeoutBwd)))) break;
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const uint4 v = make_uint4(pack2<BF16>(pr[8 * u], pr[8 * u + 1]), pack2<BF16>(pr[8 * u + 2], pr[8 * u + 3]),
@@ -610,7 +611,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       fence_async_shared();
       mbar_arrive(BAR(KV_PREADY));
       // dS^T = P^T (dP^T - delta) -> TMEM over dP^T
-      if (!(ok = mbar_wait(BAR(KV_DPFULL), s & 1, p.status, kDevTimeoutBwd))) break;
+      if (!(ok = warp_all(mbar_wait(BAR(KV_DPFULL), s & 1, p.status, kDevTimeoutBwd)))) break;
       tc_fence_after();
       uint32_t dp[2][32];
       tmem_ld32(tDPT + lane_off + 64 * w, dp[0]);
@@ -638,6 +639,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_arrive(BAR(KV_DSREADY));
     }
     if (ok) ok = mbar_wait(BAR(KV_ACC), 0, p.status, kDevTimeoutBwd);
+    ok = warp_all(ok);
     if (ok) {
       tc_fence_after();
       // warpgroup 0 writes dV rows, warpgroup 1 writes dK rows (scaled by 1/sqrt(D))

@@ -30,10 +30,11 @@
 namespace fa {
 namespace {
 
-constexpr int kThreads = 384;
-constexpr int kWarpProducerK = 8;   // Q tiles, then the K ring
-constexpr int kWarpMma = 9;
-constexpr int kWarpProducerV = 10;  // the V ring
+constexpr int kThreads = 640;
+constexpr int kSoftmaxWarps = 16;   // 4 warpgroups: tile t = wg / 2, column half h = wg % 2
+constexpr int kWarpProducerK = 16;  // Q tiles, then the K ring
+constexpr int kWarpMma = 17;
+constexpr int kWarpProducerV = 18;  // the V ring
 constexpr int kBM = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only if the max grows > 256x
@@ -45,7 +46,8 @@ struct FwdCfg {
   static constexpr int kKVChunkBytes = BN * 128;
   static constexpr int kQBytes = kBM * D * 2;
   static constexpr int kKVBytes = BN * D * 2;       // one K (or V) tile
-  static constexpr int kBudget = 225 * 1024;
+  static constexpr int kXchBytes = 2 * 2 * 2 * kBM * 4 + 2 * 2 * kBM * 4;  // row-max (x2 parity) + row-sum
+  static constexpr int kBudget = 225 * 1024 - kXchBytes;
   static constexpr int kSlots = (kBudget - 2 * kQBytes) / kKVBytes;  // K + V ring slots that fit
   static constexpr int kVStages = (kSlots / 2) > 4 ? 4 : (kSlots / 2);
   static constexpr int kKStages = (kSlots - kVStages) > 4 ? 4 : (kSlots - kVStages);
@@ -53,7 +55,8 @@ struct FwdCfg {
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = 2 * kQBytes;
   static constexpr int kOffV = kOffK + kKStages * kKVBytes;
-  static constexpr int kOffBar = kOffV + kVStages * kKVBytes;
+  static constexpr int kOffXch = kOffV + kVStages * kKVBytes;
+  static constexpr int kOffBar = kOffXch + kXchBytes;
   static constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers + 1 KiB alignment slack
 };
 
@@ -150,14 +153,19 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint64_t q_desc, uint6
   }
 }
 
-// O += P V: P (16-bit) read from TMEM as the A operand, V MN-major in shared memory.
+// O += P V: P (16-bit) read from TMEM as the A operand, V MN-major in shared memory.  P is stored
+// in two halves, one per softmax warpgroup of the tile: keys [0, BN/2) packed at S columns
+// [0, BN/4), keys [BN/2, BN) at [BN/2, BN/2 + BN/4) (each warpgroup overwrites only the first
+// half of its own S columns, which it has already read).
 template <int D, int BN, bool BF16>
 __device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint64_t v_desc,
                                          uint32_t accumulate) {
   constexpr uint32_t IDESC = idesc_f16(BF16, kBM, D, false, true);
+  constexpr int kStepsPerHalf = BN / 32;
 #pragma unroll
   for (int k = 0; k < BN / 16; ++k)
-    umma_ts(o_tmem, p_tmem + k * 8, desc_add(v_desc, k * 2048), IDESC, (accumulate | k) ? 1u : 0u);
+    umma_ts(o_tmem, p_tmem + (k / kStepsPerHalf) * (BN / 2) + (k % kStepsPerHalf) * 8,
+            desc_add(v_desc, k * 2048), IDESC, (accumulate | k) ? 1u : 0u);
 }
 
 template <int D, int BN, bool BF16>
@@ -205,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(BAR(BAR_SFULL + t), 1);
-      mbar_init(BAR(BAR_PFULL + t), 128);
+      mbar_init(BAR(BAR_PFULL + t), 256);
       mbar_init(BAR(BAR_OFULL + t), 1);
     }
     mbar_init(BAR(BAR_DRAIN), 1);
@@ -220,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= 8) {
+  if (warp >= kSoftmaxWarps) {
   if (warp == kWarpProducerK) {
     // ------------------------------------------------------------ TMA: Q once, then the K ring
     if (lane == 0) {
@@ -338,50 +346,68 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   } else {
     // ------------------------------------------------------------ softmax / epilogue
-    const int t = warp / 4;
+    // warpgroup g = warp / 4: tile t = g / 2, column half h = g % 2.  A thread owns one row
+    // (TMEM lane) and BN/2 columns; the two halves of a row exchange their partial maxima (and,
+    // at the end, their partial sums) through shared memory behind a named barrier per tile.
+    const int g = warp / 4;
+    const int t = g / 2, h = g % 2;
     if (t < w.ntiles) {
+      constexpr int HC = BN / 2;  // columns per half
       const QTile tile = w.t[t];
       const int nkv = w.nkv[t];
       const int wq = warp % 4;  // TMEM lane quarter this warp may access
       const int row = wq * 32 + lane;
       const int qrow = tile.qt * kBM + row;
       const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-      const uint32_t tS = tmem + t * 128 + lane_off;
-      const uint32_t tO = tmem + 256 + t * 128 + lane_off;
+      const uint32_t tS = tmem + t * 128 + lane_off + h * HC;
+      const uint32_t tO = tmem + 256 + t * 128 + lane_off + h * (D / 2);
+      float* xmax = reinterpret_cast<float*>(smem + C::kOffXch);           // [parity][tile][half][row]
+      float* xsum = xmax + 2 * 2 * 2 * kBM;                                // [tile][half][row]
+      const uint32_t named_bar = 1 + t;
       const float scale = p.scale_log2;
       float m_used = -INFINITY;
       float l = 0.f;
       bool ok = true;
       for (int j = 0; j < nkv; ++j) {
-        ok = mbar_wait(BAR(BAR_SFULL + t), j & 1, p.status, kDevTimeoutS);
-        if (!ok) break;
-        tc_fence_after();
-        uint32_t r[BN / 32][32];
+        ok = warp_all(mbar_wait(BAR(BAR_SFULL + t), j & 1, p.status, kDevTimeoutS));
+        uint32_t r[HC / 32][32];
+        float mx_half = -INFINITY;
+        const int kbase = j * BN + h * HC;
+        const bool masked = kbase + HC - 1 > tile.qt * kBM || kbase + HC > p.S;
+        float* xm = xmax + ((j & 1) * 2 + t) * 2 * kBM;
+        if (ok) {
+          tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + c * 32, r[c]);
+          for (int c = 0; c < HC / 32; ++c) tmem_ld32(tS + c * 32, r[c]);
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) tmem_ld_wait(r[c]);
-        const int kbase = j * BN;
-        const bool masked = kbase + BN - 1 > tile.qt * kBM || kbase + BN > p.S;
-        if (masked) {
+          for (int c = 0; c < HC / 32; ++c) tmem_ld_wait(r[c]);
+          if (masked) {
 #pragma unroll
-          for (int c = 0; c < BN / 32; ++c)
+            for (int c = 0; c < HC / 32; ++c)
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int key = kbase + c * 32 + i;
-              if (key > qrow || key >= p.S) r[c][i] = __float_as_uint(-INFINITY);
-            }
+              for (int i = 0; i < 32; ++i) {
+                const int key = kbase + c * 32 + i;
+                if (key > qrow || key >= p.S) r[c][i] = __float_as_uint(-INFINITY);
+              }
+          }
+          float mx8[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) mx8[u] = -INFINITY;
+#pragma unroll
+          for (int c = 0; c < HC / 32; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mx8[i % 8] = fmaxf(mx8[i % 8], __uint_as_float(r[c][i]));
+          mx_half = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                          fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+          // full row max: exchange with the other half (double-buffered by KV-step parity)
+          xm[h * kBM + row] = mx_half;
         }
-        // row max with 8 independent partial maxima (short dependency chains)
-        float mx8[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) mx8[u] = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i) mx8[i % 8] = fmaxf(mx8[i % 8], __uint_as_float(r[c][i]));
-        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        // every thread of the tile arrives here once per step; all leave together on failure
+        if (!named_bar_and(named_bar, 256, ok)) {
+          ok = false;
+          break;
+        }
+        const float mx = fmaxf(mx_half, xm[(1 - h) * kBM + row]);
         const float mt = mx * scale;
         const bool upd = mt > m_used + kRescaleThreshold;
         const float m_new = upd ? mt : m_used;
@@ -389,24 +415,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t scale2 = f2(scale, scale);
         const uint64_t negm2 = f2(-m_new, -m_new);
         uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
+        // exp pass: re-read each 32-column chunk from TMEM (keeps register pressure at one chunk)
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = 0; c < HC / 32; ++c) {
+          uint32_t rc[32];
+          tmem_ld32(tS + c * 32, rc);
+          tmem_ld_wait(rc);
+          if (masked) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int key = kbase + c * 32 + i;
+              if (key > qrow || key >= p.S) rc[i] = __float_as_uint(-INFINITY);
+            }
+          }
           uint32_t pk[16];
           if (masked)
-            softmax_chunk<false, BF16>(r[c], scale2, negm2, sum2, pk);
+            softmax_chunk<false, BF16>(rc, scale2, negm2, sum2, pk);
           else
-            softmax_chunk<true, BF16>(r[c], scale2, negm2, sum2, pk);
+            softmax_chunk<true, BF16>(rc, scale2, negm2, sum2, pk);
           tmem_st16(tS + c * 16, pk);
         }
         const uint64_t s01 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
-        const float sum = f2lo(s01) + f2hi(s01);
-        l = l * alpha + sum;
+        l = l * alpha + (f2lo(s01) + f2hi(s01));
         m_used = m_new;
-        // Rescale the running O of this warp's rows if any row's max moved (P V of tile j-1 is
-        // complete: it was issued before S_t(j), whose completion we waited for).
+        // Rescale this half of the running O if any row's max moved (P V of tile j-1 is complete:
+        // it was issued before S_t(j), whose completion we waited for).
         if (j > 0 && __any_sync(0xffffffffu, upd)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < D / 64; ++c) {
             uint32_t o[32];
             tmem_ld32(tO + c * 32, o);
             tmem_ld_wait(o);
@@ -419,14 +455,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         mbar_arrive(BAR(BAR_PFULL + t));
       }
+      // Row sum over both halves.  Every thread of the tile reaches this barrier, whether or not
+      // its pipeline waits succeeded, so the named-barrier count always matches.
+      xsum[(t * 2 + h) * kBM + row] = l;
+      named_bar_sync(named_bar, 256);
+      const float l_row = l + xsum[(t * 2 + 1 - h) * kBM + row];
       if (ok) ok = mbar_wait(BAR(BAR_OFULL + t), 0, p.status, kDevTimeoutO);
+      ok = warp_all(ok);
       if (ok) {
         tc_fence_after();
-        const float inv_l = 1.0f / l;
+        const float inv_l = 1.0f / l_row;
         uint8_t* orow = reinterpret_cast<uint8_t*>(p.o) +
-                        (static_cast<size_t>(tile.bh) * p.S + qrow) * (D * 2);
+                        (static_cast<size_t>(tile.bh) * p.S + qrow) * (D * 2) + h * D;
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < D / 64; ++c) {
           uint32_t o[32];
           tmem_ld32(tO + c * 32, o);
           tmem_ld_wait(o);
@@ -442,8 +484,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
           }
         }
-        if (p.lse != nullptr && qrow < p.S)
-          p.lse[static_cast<size_t>(tile.bh) * p.S + qrow] = m_used + log2f(l);
+        if (h == 0 && p.lse != nullptr && qrow < p.S)
+          p.lse[static_cast<size_t>(tile.bh) * p.S + qrow] = m_used + log2f(l_row);
       }
     }
   }

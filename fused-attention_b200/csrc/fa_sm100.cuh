@@ -138,6 +138,26 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Named barrier that also ANDs a flag over the participating threads.  Used where a group of
+// warps must leave a pipelined loop together when any of them saw a failed (timed-out) wait,
+// so that no thread is ever left waiting at a barrier its partners skipped.
+__device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred ps, pd;\n\t"
+      "setp.ne.u32 ps, %3, 0;\n\t"
+      "bar.red.and.pred pd, %1, %2, ps;\n\t"
+      "selp.u32 %0, 1, 0, pd;\n\t}\n"
+      : "=r"(r)
+      : "r"(id), "r"(nthreads), "r"(static_cast<uint32_t>(v))
+      : "memory");
+  return r != 0;
+}
+
+// Warp-uniform result of a bounded wait: lanes of a warp must agree before warp-collective
+// tcgen05 instructions, even in the (failure-only) case where their waits ended differently.
+__device__ __forceinline__ bool warp_all(bool v) { return __all_sync(0xffffffffu, v) != 0; }
+
 // ---------------------------------------------------------------- TMA
 // L2 cache-policy operands for .L2::cache_hint (createpolicy results).
 __device__ __forceinline__ uint64_t policy_evict_first() {
