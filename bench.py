@@ -194,7 +194,11 @@ def main():
     dev = torch.device("cuda", local)
     group = None
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        # NCCL's blocks must get SMs while the attention kernels are queued, or the gathers of
+        # one chunk cannot overlap the kernels of the next
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = True
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev, pg_options=opts)
         group = dist.group.WORLD
 
     from attention.backward.fused_backward import fused_attention_autograd, _forward, _native

@@ -59,14 +59,27 @@ def _forward(q, k, v, tile_m, tile_n):
     return o, lse
 
 
-def _backward(q, k, v, o, lse, do, tile_m, tile_n):
+def _backward_kv(q, k, v, o, lse, do, tile_m, tile_n):
+    """First half of _backward: delta = rowsum(dO * O), then dK and dV.  Returns (delta, dk, dv)."""
     B, H, N, D = q.shape
     nat = _native()
     delta = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dk, dv = torch.empty_like(k), torch.empty_like(v)
     nat.bwd_preprocess(o, do, delta)
     nat.bwd_dkdv(q, k, v, do, lse, delta, dk, dv, tile_m, tile_n)
-    nat.bwd_dq(q, k, v, do, lse, delta, dq, tile_m, tile_n)
+    return delta, dk, dv
+
+
+def _backward_q(q, k, v, do, lse, delta, tile_m, tile_n):
+    """Second half of _backward: dQ from the delta of _backward_kv."""
+    dq = torch.empty_like(q)
+    _native().bwd_dq(q, k, v, do, lse, delta, dq, tile_m, tile_n)
+    return dq
+
+
+def _backward(q, k, v, o, lse, do, tile_m, tile_n):
+    delta, dk, dv = _backward_kv(q, k, v, o, lse, do, tile_m, tile_n)
+    dq = _backward_q(q, k, v, do, lse, delta, tile_m, tile_n)
     return dq, dk, dv
 
 

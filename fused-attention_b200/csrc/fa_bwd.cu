@@ -206,7 +206,7 @@ struct DqCfg {
 
 enum : int {
   DQ_OUTER = 0, DQ_KFULL = 1, DQ_KEMPTY = 5, DQ_VFULL = 9, DQ_VEMPTY = 13, DQ_SFULL = 17, DQ_SFREE = 18,
-  DQ_DPFULL = 19 /* + 2 */, DQ_DSREADY = 21, DQ_ACC = 22, DQ_DRAIN = 23
+  DQ_DPFULL = 19 /* + 2 */, DQ_DSREADY = 21 /* + 2 */, DQ_ACC = 23, DQ_DRAIN = 24
 };
 
 template <int D, bool BF16>
@@ -235,7 +235,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(BAR(DQ_SFREE), 256);
     mbar_init(BAR(DQ_DPFULL + 0), 1);
     mbar_init(BAR(DQ_DPFULL + 1), 1);
-    mbar_init(BAR(DQ_DSREADY), 256);
+    mbar_init(BAR(DQ_DSREADY + 0), 256);
+    mbar_init(BAR(DQ_DSREADY + 1), 256);
     mbar_init(BAR(DQ_ACC), 1);
     mbar_init(BAR(DQ_DRAIN), 1);
     fence_barrier_init();
@@ -327,7 +328,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             umma_commit(BAR(DQ_DPFULL + ((s + 1) & 1)));
             umma_commit(BAR(DQ_VEMPTY + v1));
           }
-          if (!(ok = mbar_wait(BAR(DQ_DSREADY), s & 1, p.status, kDevTimeoutBwd))) break;
+          // dS(s) is ready.  One barrier per step parity: S(s+1) and dP(s+1) are already issued,
+          // so the compute warps can finish step s+1 before this thread looks, and a single
+          // barrier would then be two phases ahead of the parity waited on.
+          if (!(ok = mbar_wait(BAR(DQ_DSREADY + (s & 1)), (s >> 1) & 1, p.status, kDevTimeoutBwd))) break;
           tc_fence_after();
           umma_tmem_tile<D, BF16>(tDQ, tDP + 128 * (s & 1), desc_add(dKm, (s % KST) * C::kTile), s > 0 ? 1u : 0u);
           umma_commit(BAR(DQ_KEMPTY + s % KST));
@@ -391,7 +395,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(BAR(DQ_DSREADY));
+      mbar_arrive(BAR(DQ_DSREADY + (s & 1)));
     }
     if (ok) ok = mbar_wait(BAR(DQ_ACC), 0, p.status, kDevTimeoutBwd);
     ok = warp_all(ok);

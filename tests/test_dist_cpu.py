@@ -51,7 +51,15 @@ def _cpu_kernels():
             attn32(qf, kf, vf)[0].backward(do.float())
         return qf.grad.to(q.dtype), kf.grad.to(k.dtype), vf.grad.to(v.dtype)
 
-    return types.SimpleNamespace(_check=real._check, _forward=_forward, _backward=_backward)
+    def _backward_kv(q, k, v, o, lse, do, tm, tn):
+        dq, dk, dv = _backward(q, k, v, o, lse, do, tm, tn)
+        return dq, dk, dv  # the dQ of the double stands in for delta
+
+    def _backward_q(q, k, v, do, lse, delta, tm, tn):
+        return delta
+
+    return types.SimpleNamespace(_check=real._check, _forward=_forward, _backward=_backward,
+                                 _backward_kv=_backward_kv, _backward_q=_backward_q)
 
 
 def _inputs(B, H, H_kv, S, D):
@@ -63,7 +71,7 @@ def _inputs(B, H, H_kv, S, D):
     return q, k, v, do
 
 
-def _worker(rank, world, port, shape, result_path):
+def _worker(rank, world, port, shape, result_path, min_units=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     import sys
@@ -71,6 +79,8 @@ def _worker(rank, world, port, shape, result_path):
     from attention import dist as adist
     fake = _cpu_kernels()
     adist._backward_module = lambda: fake
+    if min_units is not None:
+        adist.MIN_UNITS_PER_CHUNK = min_units
     q, k, v, do = _inputs(*shape)
     qg, kg, vg = (t.clone().requires_grad_(True) for t in (q, k, v))
     o = adist.sharded_attention_autograd(qg, kg, vg, 64, 64)
@@ -81,12 +91,15 @@ def _worker(rank, world, port, shape, result_path):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("shape", [(2, 4, 4, 128, 64), (1, 8, 2, 128, 64), (2, 4, 1, 64, 64)],
-                         ids=["mha_batch_split", "gqa_head_split", "mqa"])
-def test_sharded_matches_single_process(shape, tmp_path):
+@pytest.mark.parametrize("shape,min_units", [
+    ((2, 4, 4, 128, 64), None), ((1, 8, 2, 128, 64), None), ((2, 4, 1, 64, 64), None),
+    ((4, 4, 4, 64, 64), 1), ((4, 8, 2, 64, 64), 2)],
+    ids=["mha_batch_split", "gqa_head_split", "mqa", "mha_4_chunks", "gqa_2_chunks"])
+def test_sharded_matches_single_process(shape, min_units, tmp_path):
     world = 2
     out = str(tmp_path / "r0.pt")
-    mp.start_processes(_worker, args=(world, _free_port(), shape, out), nprocs=world, start_method="spawn")
+    mp.start_processes(_worker, args=(world, _free_port(), shape, out, min_units), nprocs=world,
+                       start_method="spawn")
     got = torch.load(out)
     fake = _cpu_kernels()
     q, k, v, do = _inputs(*shape)
@@ -104,6 +117,28 @@ def test_shard_units():
     assert shard_units(1, 8, 2, 1) == (4, 8)
     with pytest.raises(ValueError):
         shard_units(1, 3, 2, 0)
+
+
+def test_chunk_layout():
+    """Chunk c of all ranks, in rank order, is one contiguous slab; all chunks cover every unit
+    exactly once."""
+    import sys
+    sys.path.insert(0, os.path.join(REPO, "fused-attention_b200"))
+    from attention.dist import chunk_ranges, plan_chunks
+    assert plan_chunks(128 * 8, 8) == 4 and plan_chunks(16, 2) == 1 and plan_chunks(32, 2) == 2
+    with pytest.raises(ValueError):
+        plan_chunks(10, 4)
+    for units, world in ((1024, 8), (96, 2), (64, 4), (8, 8)):
+        chunks = plan_chunks(units, world)
+        per_rank = [chunk_ranges(units, world, r, chunks) for r in range(world)]
+        span = units // world // chunks * world
+        seen = []
+        for c in range(chunks):
+            runs = [per_rank[r][c] for r in range(world)]
+            assert runs[0][0] == c * span and runs[-1][1] == (c + 1) * span
+            assert all(runs[r][1] == runs[r + 1][0] for r in range(world - 1))
+            seen += [u for a, b in runs for u in range(a, b)]
+        assert sorted(seen) == list(range(units))
 
 
 def _failing_worker(rank, world, port, flag_path):

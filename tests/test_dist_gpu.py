@@ -23,7 +23,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, shape, out_path):
+def _worker(rank, world, port, shape, out_path, min_units=None):
     import sys
     from datetime import timedelta
     sys.path.insert(0, os.path.join(REPO, "fused-attention_b200"))
@@ -31,8 +31,14 @@ def _worker(rank, world, port, shape, out_path):
     import torch.distributed as dist
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    opts = dist.ProcessGroupNCCL.Options()
+    opts.is_high_priority_stream = True
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev,
+                            pg_options=opts)
+    from attention import dist as adist
     from attention.dist import sharded_attention_autograd
+    if min_units is not None:
+        adist.MIN_UNITS_PER_CHUNK = min_units
     from attention.backward.fused_backward import fused_attention_autograd
     B, H, H_kv, S, D = shape
     g = torch.Generator(device=dev).manual_seed(7)
@@ -57,10 +63,12 @@ def _worker(rank, world, port, shape, out_path):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("shape", [(2, 8, 8, 1024, 128), (1, 8, 2, 2048, 64)], ids=["mha_batch", "gqa_heads"])
-def test_sharded_matches_single_gpu(shape, tmp_path):
+@pytest.mark.parametrize("shape,min_units", [((2, 8, 8, 1024, 128), None), ((1, 8, 2, 2048, 64), None),
+                                              ((4, 8, 8, 1024, 128), 2), ((4, 8, 4, 1024, 64), 1)],
+                         ids=["mha_batch", "gqa_heads", "mha_4_chunks", "gqa_4_chunks"])
+def test_sharded_matches_single_gpu(shape, min_units, tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     out = str(tmp_path / "result.txt")
-    mp.start_processes(_worker, args=(2, _free_port(), shape, out), nprocs=2, start_method="spawn")
+    mp.start_processes(_worker, args=(2, _free_port(), shape, out, min_units), nprocs=2, start_method="spawn")
     assert open(out).read() == "same"
