@@ -51,28 +51,30 @@ def _check(q, k, v, tile_m, tile_n):
         raise ValueError(f"N={N} must be divisible by tile_m={tile_m} and tile_n={tile_n}")
 
 
-def _forward(q, k, v, tile_m, tile_n):
+def _forward(q, k, v, tile_m, tile_n, out=None):
     B, H, N, D = q.shape
-    o = torch.empty_like(q)
+    o = torch.empty_like(q) if out is None else out
     lse = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
     _native().fwd(q, k, v, o, lse, tile_m, tile_n)
     return o, lse
 
 
-def _backward_kv(q, k, v, o, lse, do, tile_m, tile_n):
-    """First half of _backward: delta = rowsum(dO * O), then dK and dV.  Returns (delta, dk, dv)."""
+def _backward_kv(q, k, v, o, lse, do, tile_m, tile_n, dk=None, dv=None):
+    """First half of _backward: delta = rowsum(dO * O), then dK and dV (into dk / dv when given,
+    contiguous tensors shaped like k).  Returns (delta, dk, dv)."""
     B, H, N, D = q.shape
     nat = _native()
     delta = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
-    dk, dv = torch.empty_like(k), torch.empty_like(v)
+    dk = torch.empty_like(k) if dk is None else dk
+    dv = torch.empty_like(v) if dv is None else dv
     nat.bwd_preprocess(o, do, delta)
     nat.bwd_dkdv(q, k, v, do, lse, delta, dk, dv, tile_m, tile_n)
     return delta, dk, dv
 
 
-def _backward_q(q, k, v, do, lse, delta, tile_m, tile_n):
-    """Second half of _backward: dQ from the delta of _backward_kv."""
-    dq = torch.empty_like(q)
+def _backward_q(q, k, v, do, lse, delta, tile_m, tile_n, dq=None):
+    """Second half of _backward: dQ (into dq when given) from the delta of _backward_kv."""
+    dq = torch.empty_like(q) if dq is None else dq
     _native().bwd_dq(q, k, v, do, lse, delta, dq, tile_m, tile_n)
     return dq
 

@@ -11,16 +11,22 @@ consecutive units is ONE contiguous slab of every tensor.  Consequences:
 
 Pipelining.  A rank's units are split into C chunks, and chunk c of rank r is the run of units
 [(c * W + r) * cs, (c * W + r + 1) * cs) (W ranks, cs units per chunk).  Chunk c of all ranks
-together is then the contiguous slab [c * W * cs, (c + 1) * W * cs), so its all-gather can be
-issued as soon as chunk c is computed and runs on a side stream while chunk c + 1 computes.
-With C = 1 this is the plain contiguous split.  Only the last chunk's gathers are exposed.
+together is then the contiguous slab [c * W * cs, (c + 1) * W * cs), so it can be gathered as soon
+as chunk c is computed, on a side stream, while chunk c + 1 computes.  With C = 1 this is the plain
+contiguous split.  The kernels write a rank's own chunk straight into the full output tensor.
 
-The only collectives are the all-gathers of O (forward) and of dQ, dK, dV (backward), and every
-rank issues them in the same order.  They overlap the kernels only if NCCL's blocks get SMs while
-the attention kernels (one CTA per SM) are queued: create the process group with
-ProcessGroupNCCL.Options(is_high_priority_stream=True), as bench.py does.  Each rank holds the
-full inputs (replicated) and receives the full outputs, which is the drop-in semantics of the
-single-GPU functions.  Requires (B * H_kv) % world_size == 0.
+Gathering a chunk (CUDA, the default "pull" mode): each rank copies its chunk into a staging area
+of symmetric memory (every rank's staging area is mapped into every other rank), a one-element
+NCCL all-reduce on the side stream acts as the barrier "every rank has staged chunk c", and each
+rank then pulls the W - 1 other chunks from the peers' staging areas with plain device-to-device
+copies, which run on the copy engines and take no SMs away from the attention kernels.  A final
+barrier keeps the staging area from being overwritten before every peer has read it.  With
+FA_GATHER=nccl (and always on CPU / gloo) a chunk is gathered with all_gather_into_tensor
+instead; the NCCL kernels then compete with the attention kernels for SMs.
+
+Every rank issues the same collectives in the same order.  Each rank holds the full inputs
+(replicated) and receives the full outputs, which is the drop-in semantics of the single-GPU
+functions.  Requires (B * H_kv) % world_size == 0.
 """
 import importlib.util
 import os
@@ -86,10 +92,12 @@ def _unit_view(t, H_kv):
 
 
 _COMM_STREAMS = {}
+_WORKSPACES = {}
+_FLAGS = {}
 
 
 def _comm_stream(device):
-    """One high-priority side stream per device for the all-gathers."""
+    """One high-priority side stream per device for the gathers."""
     s = _COMM_STREAMS.get(device)
     if s is None:
         s = torch.cuda.Stream(device=device, priority=-1)
@@ -97,37 +105,107 @@ def _comm_stream(device):
     return s
 
 
+def _group_name(group):
+    return (group if group is not None else dist.group.WORLD).group_name
+
+
+def _workspace(device, group, nbytes):
+    """Symmetric staging memory of at least `nbytes` on every rank of `group` (collective when it
+    has to grow: every rank asks for the same size at the same point)."""
+    key = (device, _group_name(group))
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws[0].numel() < nbytes:
+        import torch.distributed._symmetric_memory as symm_mem
+        size = max(nbytes, ws[0].numel() if ws is not None else 0)
+        buf = symm_mem.empty(size, dtype=torch.uint8, device=device)
+        handle = symm_mem.rendezvous(buf, _group_name(group))
+        old = ws
+        ws = (buf, handle, old)  # a replaced area stays mapped: peers may still hold its address
+        _WORKSPACES[key] = ws
+    return ws[1]
+
+
+def _flag(device):
+    f = _FLAGS.get(device)
+    if f is None:
+        f = torch.zeros(1, dtype=torch.int32, device=device)
+        _FLAGS[device] = f
+    return f
+
+
+def gather_mode(device):
+    if device.type != "cuda":
+        return "nccl"
+    mode = os.environ.get("FA_GATHER", "pull")
+    if mode not in ("pull", "nccl"):
+        raise ValueError(f"FA_GATHER must be 'pull' or 'nccl', not {mode!r}")
+    return mode
+
+
 class _Gathers:
-    """Issues all-gathers of finished chunks on a side stream (CUDA) or inline (CPU/gloo).
+    """The gathers of one forward or backward pass.
 
-    Tensors handed to a gather stay referenced until finish(), after which the caller's stream
-    is ordered after every gather: no buffer is reused while NCCL may still read or write it."""
+    gather(items) takes (slab, local, stage_offset) triples: `slab` is the output slab of one
+    chunk (W * cs units), `local` is this rank's cs units, which the kernels already wrote into
+    the rank's slot of the slab, and `stage_offset` is where the chunk goes in the staging area
+    (the same on every rank).  Tensors handed over stay referenced until finish(), after which
+    the caller's stream is ordered after every copy: no buffer is reused while a peer or NCCL may
+    still read or write it."""
 
-    def __init__(self, device, group):
+    def __init__(self, device, group, stage_bytes):
         self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
         self.cuda = device.type == "cuda"
+        self.mode = gather_mode(device)
         self.keep = []
         if self.cuda:
             self.compute = torch.cuda.current_stream(device)
             self.comm = _comm_stream(device)
+        if self.mode == "pull":
+            self.handle = _workspace(device, group, stage_bytes)
+            self.flag = _flag(device)
 
-    def gather(self, pairs):
+    def _barrier(self):
+        dist.all_reduce(self.flag, group=self.group)
+
+    def gather(self, items):
         if not self.cuda:
-            for out, inp in pairs:
-                dist.all_gather_into_tensor(out, inp, group=self.group)
+            for slab, local, _ in items:
+                dist.all_gather_into_tensor(slab, local, group=self.group)
             return
         ready = torch.cuda.Event()
         ready.record(self.compute)
         with torch.cuda.stream(self.comm):
             self.comm.wait_event(ready)
-            for out, inp in pairs:
-                dist.all_gather_into_tensor(out, inp, group=self.group)
-        self.keep.extend(t for pair in pairs for t in pair)
+            if self.mode == "nccl":
+                for slab, local, _ in items:
+                    dist.all_gather_into_tensor(slab, local, group=self.group)
+            else:
+                for _, local, off in items:
+                    self.handle.get_buffer(self.rank, tuple(local.shape), local.dtype,
+                                           off // local.element_size()).copy_(local)
+                self._barrier()
+                for slab, local, off in items:
+                    cs = local.shape[0]
+                    for step in range(1, self.world):
+                        peer = (self.rank + step) % self.world
+                        src = self.handle.get_buffer(peer, tuple(local.shape), local.dtype,
+                                                     off // local.element_size())
+                        slab[peer * cs:(peer + 1) * cs].copy_(src)
+        self.keep.extend(t for slab, local, _ in items for t in (slab, local))
 
     def finish(self):
         if self.cuda:
+            if self.mode == "pull":
+                with torch.cuda.stream(self.comm):
+                    self._barrier()
             self.compute.wait_stream(self.comm)
         self.keep.clear()
+
+
+def _nbytes(t):
+    return t.numel() * t.element_size()
 
 
 class ShardedFusedAttentionFn(torch.autograd.Function):
@@ -142,43 +220,48 @@ class ShardedFusedAttentionFn(torch.autograd.Function):
         units = q.shape[0] * H_kv
         chunks = plan_chunks(units, world)
         ranges = chunk_ranges(units, world, rank, chunks)
+        span = (units // world // chunks) * world  # units per gathered slab
         qu, ku, vu = _unit_view(q, H_kv), _unit_view(k, H_kv), _unit_view(v, H_kv)
         o = torch.empty_like(q)
         ou = _unit_view(o, H_kv)
-        span = (units // world // chunks) * world  # units per gathered slab
-        gathers = _Gathers(q.device, group)
-        saved = []
+        chunk_bytes = _nbytes(ou[:span // world])
+        gathers = _Gathers(q.device, group, chunks * chunk_bytes)
+        lses = []
         for c, (a, b) in enumerate(ranges):
-            ol, lse = fb._forward(qu[a:b], ku[a:b], vu[a:b], tile_m, tile_n)
-            gathers.gather([(ou[c * span:(c + 1) * span], ol)])
-            saved += [ol, lse]
+            _, lse = fb._forward(qu[a:b], ku[a:b], vu[a:b], tile_m, tile_n, out=ou[a:b])
+            gathers.gather([(ou[c * span:(c + 1) * span], ou[a:b], c * chunk_bytes)])
+            lses.append(lse)
         gathers.finish()
-        ctx.save_for_backward(q, k, v, *saved)
+        ctx.save_for_backward(q, k, v, o, *lses)
         ctx.meta = (tile_m, tile_n, group, H_kv, ranges, span)
         return o
 
     @staticmethod
     def backward(ctx, do):
         fb = _backward_module()
-        q, k, v, *saved = ctx.saved_tensors
+        q, k, v, o, *lses = ctx.saved_tensors
         tile_m, tile_n, group, H_kv, ranges, span = ctx.meta
         do = do.contiguous()
         if do.dtype != q.dtype:
             do = do.to(q.dtype)
-        qu, ku, vu, dou = (_unit_view(t, H_kv) for t in (q, k, v, do))
+        qu, ku, vu, ou, dou = (_unit_view(t, H_kv) for t in (q, k, v, o, do))
         dq = torch.empty(q.shape, device=do.device, dtype=do.dtype)
         dk = torch.empty(k.shape, device=do.device, dtype=do.dtype)
         dv = torch.empty(k.shape, device=do.device, dtype=do.dtype)
         dqu, dku, dvu = (_unit_view(t, H_kv) for t in (dq, dk, dv))
-        gathers = _Gathers(do.device, group)
+        chunks = len(ranges)
+        cq = _nbytes(dqu[ranges[0][0]:ranges[0][1]])
+        ckv = _nbytes(dku[ranges[0][0]:ranges[0][1]])
+        off_k, off_v, off_q = 0, chunks * ckv, 2 * chunks * ckv  # staging: dK chunks | dV | dQ
+        gathers = _Gathers(do.device, group, 2 * chunks * ckv + chunks * cq)
         for c, (a, b) in enumerate(ranges):
-            ol, lse = saved[2 * c], saved[2 * c + 1]
             sl = slice(c * span, (c + 1) * span)
             # dK, dV of this chunk travel while its dQ kernel runs
-            delta, dkl, dvl = fb._backward_kv(qu[a:b], ku[a:b], vu[a:b], ol, lse, dou[a:b], tile_m, tile_n)
-            gathers.gather([(dku[sl], dkl), (dvu[sl], dvl)])
-            dql = fb._backward_q(qu[a:b], ku[a:b], vu[a:b], dou[a:b], lse, delta, tile_m, tile_n)
-            gathers.gather([(dqu[sl], dql)])
+            delta, _, _ = fb._backward_kv(qu[a:b], ku[a:b], vu[a:b], ou[a:b], lses[c], dou[a:b],
+                                          tile_m, tile_n, dk=dku[a:b], dv=dvu[a:b])
+            gathers.gather([(dku[sl], dku[a:b], off_k + c * ckv), (dvu[sl], dvu[a:b], off_v + c * ckv)])
+            fb._backward_q(qu[a:b], ku[a:b], vu[a:b], dou[a:b], lses[c], delta, tile_m, tile_n, dq=dqu[a:b])
+            gathers.gather([(dqu[sl], dqu[a:b], off_q + c * cq)])
         gathers.finish()
         return dq, dk, dv, None, None, None
 

@@ -41,8 +41,11 @@ def _cpu_kernels():
         s = s.masked_fill(torch.ones(n, n, dtype=torch.bool).triu(1), float("-inf"))
         return torch.softmax(s, -1) @ v, torch.logsumexp(s, -1) * 1.4426950408889634
 
-    def _forward(q, k, v, tm, tn):
+    def _forward(q, k, v, tm, tn, out=None):
         o, lse = attn32(q.float(), k.float(), v.float())
+        if out is not None:
+            out.copy_(o)
+            return out, lse
         return o.to(q.dtype), lse
 
     def _backward(q, k, v, o, lse, do, tm, tn):
@@ -51,11 +54,16 @@ def _cpu_kernels():
             attn32(qf, kf, vf)[0].backward(do.float())
         return qf.grad.to(q.dtype), kf.grad.to(k.dtype), vf.grad.to(v.dtype)
 
-    def _backward_kv(q, k, v, o, lse, do, tm, tn):
-        dq, dk, dv = _backward(q, k, v, o, lse, do, tm, tn)
-        return dq, dk, dv  # the dQ of the double stands in for delta
+    def _backward_kv(q, k, v, o, lse, do, tm, tn, dk=None, dv=None):
+        dq_, dk_, dv_ = _backward(q, k, v, o, lse, do, tm, tn)
+        if dk is not None:
+            dk.copy_(dk_), dv.copy_(dv_)
+            dk_, dv_ = dk, dv
+        return dq_, dk_, dv_  # the dQ of the double stands in for delta
 
-    def _backward_q(q, k, v, do, lse, delta, tm, tn):
+    def _backward_q(q, k, v, do, lse, delta, tm, tn, dq=None):
+        if dq is not None:
+            return dq.copy_(delta)
         return delta
 
     return types.SimpleNamespace(_check=real._check, _forward=_forward, _backward=_backward,

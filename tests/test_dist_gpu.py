@@ -23,11 +23,11 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, shape, out_path, min_units=None):
+def _worker(rank, world, port, shape, out_path, min_units=None, mode="pull"):
     import sys
     from datetime import timedelta
     sys.path.insert(0, os.path.join(REPO, "fused-attention_b200"))
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0", FA_GATHER=mode)
     import torch.distributed as dist
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -63,12 +63,14 @@ def _worker(rank, world, port, shape, out_path, min_units=None):
     dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("mode", ["pull", "nccl"])
 @pytest.mark.parametrize("shape,min_units", [((2, 8, 8, 1024, 128), None), ((1, 8, 2, 2048, 64), None),
                                               ((4, 8, 8, 1024, 128), 2), ((4, 8, 4, 1024, 64), 1)],
                          ids=["mha_batch", "gqa_heads", "mha_4_chunks", "gqa_4_chunks"])
-def test_sharded_matches_single_gpu(shape, min_units, tmp_path):
+def test_sharded_matches_single_gpu(shape, min_units, mode, tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     out = str(tmp_path / "result.txt")
-    mp.start_processes(_worker, args=(2, _free_port(), shape, out, min_units), nprocs=2, start_method="spawn")
+    mp.start_processes(_worker, args=(2, _free_port(), shape, out, min_units, mode), nprocs=2,
+                       start_method="spawn")
     assert open(out).read() == "same"
