@@ -67,6 +67,15 @@ def load_peaks():
         return FALLBACK_PEAK, 6650.0, "fallback"
 
 
+def load_sustained_peak():
+    """cuBLAS bf16 TFLOP/s back to back for seconds under the power cap (MEASURED_PEAKS.json)."""
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops_sustained"])
+    except (OSError, ValueError, KeyError):
+        return None
+
+
 def load_traffic():
     """Per-launch DRAM bytes of each kernel from the committed ncu summary (or None)."""
     path = os.path.join(REPO, "profiles", "traffic.txt")
@@ -301,8 +310,11 @@ def main():
     dom_flops = kern[dominant][1] * shard_unit_flops
     achieved = dom_flops / (kt[dominant] / 1e3) / 1e12
     traffic = load_traffic().get((dominant, f"S{S}_D{D}"))
+    sustained = load_sustained_peak()
     roofline = {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": peak, "unit": UNIT,
                 "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
+                # the power-capped cuBLAS figure: what a tensor-bound kernel inside a long step meets
+                "peak_sustained": sustained, "frac_sustained": (achieved / sustained) if sustained else None,
                 "algorithmic_flops_per_launch": dom_flops, "launch_ms": kt[dominant],
                 "kernels_ms": kt,
                 "kernels_tflops": {n: (kern[n][1] * shard_unit_flops / (kt[n] / 1e3) / 1e12) if kern[n][1] else None

@@ -64,16 +64,22 @@ def shard_units(B, H_kv, world, rank):
 
 # Fewer units than this per chunk would leave too few CTAs per launch to fill 148 SMs.
 MIN_UNITS_PER_CHUNK = 8
-MAX_CHUNKS = 4
+
+
+def max_chunks(world):
+    """The copy engines sit idle while a pass computes its first chunk and the last chunk's
+    copies run after the kernels: finer chunks shorten both, at the price of more, smaller
+    launches.  The gathered bytes per rank grow with world - 1, so larger worlds take more."""
+    return 8 if world >= 4 else 4
 
 
 def plan_chunks(units, world):
-    """Number of chunks C per rank: the largest of MAX_CHUNKS, ..., 2 that divides the rank's
-    units with at least MIN_UNITS_PER_CHUNK units per chunk, else 1."""
+    """Number of chunks C per rank: the largest of max_chunks(world), ..., 2 that divides the
+    rank's units with at least MIN_UNITS_PER_CHUNK units per chunk, else 1."""
     if units % world:
         raise ValueError(f"B * H_kv = {units} units cannot be split evenly over {world} ranks")
     per = units // world
-    for c in range(MAX_CHUNKS, 1, -1):
+    for c in range(max_chunks(world), 1, -1):
         if per % c == 0 and per // c >= MIN_UNITS_PER_CHUNK:
             return c
     return 1
