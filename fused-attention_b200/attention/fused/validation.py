@@ -3,7 +3,7 @@
 Mirrors the reference's `attention/fused/validation.py:37-88` (same function, exception type
 and message wording) with the limits the B200 kernels support:
   Q, K, V: [B, H, N, D], contiguous, all float16 or all bfloat16 (the reference: float16 only)
-  1 <= B <= 16, 1 <= H <= 32, 1 <= N <= 32768 (the reference: 8192), D in {64, 128}
+  1 <= B <= 16, 1 <= H <= 32, 1 <= N <= 32768 (the reference: 8192), D in {32, 64, 128}
   N divisible by the query tile (block_m) and key tile (block_n)
 Works on NumPy arrays and torch tensors (anything with .shape and .dtype).
 """
@@ -11,7 +11,7 @@ Works on NumPy arrays and torch tensors (anything with .shape and .dtype).
 MAX_BATCH = 16
 MAX_HEADS = 32
 MAX_SEQ_LEN = 32768
-SUPPORTED_HEAD_DIMS = (64, 128)
+SUPPORTED_HEAD_DIMS = (32, 64, 128)
 SUPPORTED_DTYPES = ("float16", "bfloat16")
 
 

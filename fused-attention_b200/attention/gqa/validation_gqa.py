@@ -2,7 +2,7 @@
 
 Mirrors the reference's `attention/gqa/validation_gqa.py:39-104` (same function, exception type,
 messages and return value: the group size H // H_kv) with the B200 limits of
-`attention/fused/validation.py` (float16 or bfloat16, N <= 32768, D in {64, 128}).
+`attention/fused/validation.py` (float16 or bfloat16, N <= 32768, D in {32, 64, 128}).
   Q: [B, H, N, D]   K, V: [B, H_kv, N, D]   1 <= H_kv <= H, H % H_kv == 0
 """
 import importlib.util

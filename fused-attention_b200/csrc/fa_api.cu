@@ -47,12 +47,15 @@ int make_map(CUtensorMap* m, const void* ptr, int bh, int S, int D, int dtype, i
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S),
                         static_cast<cuuint64_t>(bh)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(S) * D * 2};
-  cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(box_rows), 1u};
+  // 64-column boxes (128-byte rows) with the 128-byte swizzle; D = 32 rows are 64 bytes, so
+  // one 32-column box with the 64-byte swizzle.
+  const bool narrow = D < 64;
+  cuuint32_t box[3] = {narrow ? 32u : 64u, static_cast<cuuint32_t>(box_rows), 1u};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   CUresult r = enc(m, dtype == FA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                    3, const_cast<void*>(ptr), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, narrow ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? FA_OK : FA_ERR_DRIVER;
 }
@@ -79,7 +82,7 @@ int check_common(int B, int H, int H_kv, int S, int D, int dtype, int tile_m, in
   if (H % H_kv != 0) return FA_ERR_INVALID_ARG;
   if (dev_status == nullptr) return FA_ERR_INVALID_ARG;
   if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_ERR_UNSUPPORTED;
-  if (D != 64 && D != 128) return FA_ERR_UNSUPPORTED;
+  if (D != 32 && D != 64 && D != 128) return FA_ERR_UNSUPPORTED;
   if ((tile_m != 64 && tile_m != 128) || (tile_n != 64 && tile_n != 128)) return FA_ERR_UNSUPPORTED;
   // Every index the kernels form fits in 32 bits per head, 64 bits overall.
   if (static_cast<long long>(B) * H > (1LL << 30) || S > (1 << 24)) return FA_ERR_UNSUPPORTED;
@@ -96,7 +99,7 @@ const char* fa_strerror(int code) {
   switch (code) {
     case FA_OK: return "ok";
     case FA_ERR_INVALID_ARG: return "invalid argument (null pointer, non-positive size or H not divisible by H_kv)";
-    case FA_ERR_UNSUPPORTED: return "unsupported configuration (D must be 64 or 128, dtype f16/bf16, tiles 64/128)";
+    case FA_ERR_UNSUPPORTED: return "unsupported configuration (D must be 32, 64 or 128 in the forward and 64 or 128 in the backward, dtype f16/bf16, tiles 64/128)";
     case FA_ERR_ALIGNMENT: return "tensor base address is not 16-byte aligned";
     case FA_ERR_CUDA: return "CUDA runtime error (see fa_last_cuda_error)";
     case FA_ERR_DRIVER: return "cuTensorMapEncodeTiled unavailable or rejected the tensor";
@@ -147,6 +150,7 @@ int fa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int
 int fa_bwd_preprocess(const void* o, const void* dO, float* delta, int B, int H, int S, int D,
                       int dtype, int* dev_status, void* stream) {
   if (!o || !dO || !delta) return FA_ERR_INVALID_ARG;
+  if (D == 32) return FA_ERR_UNSUPPORTED;  // the backward kernels take D = 64 or 128
   int rc = check_common(B, H, H, S, D, dtype, 128, 128, dev_status);
   if (rc != FA_OK) return rc;
   if (!aligned16(o) || !aligned16(dO) || (reinterpret_cast<uintptr_t>(delta) & 3u))
@@ -172,6 +176,7 @@ static int bwd_prepare(const void* q, const void* k, const void* v, const void* 
                        CUtensorMap* tmQ, CUtensorMap* tmK, CUtensorMap* tmV, CUtensorMap* tmdO,
                        fa::BwdParams* p, int q_rows, int kv_rows) {
   if (!q || !k || !v || !dO || !lse || !delta) return FA_ERR_INVALID_ARG;
+  if (D == 32) return FA_ERR_UNSUPPORTED;  // the backward kernels take D = 64 or 128
   int rc = check_common(B, H, H_kv, S, D, dtype, tile_m, tile_n, dev_status);
   if (rc != FA_OK) return rc;
   // The backward streams whole 64-row tiles (and their lse / delta slices).

@@ -57,14 +57,15 @@ cudaError_t launch_pre_t(const BwdParams& p, cudaStream_t stream) {
 //          TMEM: dQ | S | dP[0] | dP[1].  S is released as soon as both compute warpgroups have
 //          read it, so S(s+1) runs on the tensor core while P(s) is being computed; dS overwrites
 //          the first half of each warpgroup's own dP columns and feeds dQ += dS K from TMEM.
-//   dK/dV: CTA = 128 keys of one K/V head (K, V resident); streams 128-row Q / dO tiles (and
-//          their LSE / delta slices) of every query head of the GQA group, from the diagonal on
-//          (reference loop: attention/backward/fused_backward.py:81-103).
-//          TMEM: dV | dK | S^T | dP^T.  S^T is released on read; P^T goes to shared memory in
-//          the 128-byte-swizzled K-major layout the tensor core reads as an A operand, so the next
-//          S^T overlaps the exp work; dS^T overwrites dP^T and feeds dK += dS^T Q from TMEM.
+//   dK/dV: CTA = 128 keys of one K/V head (K, V resident); streams 128-row Q tiles (with their
+//          LSE slices, 3-stage ring) and dO tiles (with their delta slices, 2-stage ring) of
+//          every query head of the GQA group, from the diagonal on (reference loop:
+//          attention/backward/fused_backward.py:81-103).  TMEM: dV | dK | S^T | dP^T.  P^T
+//          overwrites S^T and dS^T overwrites dP^T, and both feed their UMMAs (dV += P^T dO,
+//          dK += dS^T Q) straight from TMEM, which leaves the shared memory for a third Q stage:
+//          Q(s) is held until dK(s), so with two stages the next tile's load was exposed.
 // Warp roles (384 threads): warps 0-3 and 4-7 are two compute warpgroups splitting every tile's
-// 128 columns (each thread: one TMEM lane = one row, 64 columns); warp 8 (and 10 in dQ) issue TMA
+// 128 columns (each thread: one TMEM lane = one row, 64 columns); warps 8 and 10 issue TMA
 // loads; warp 9 is the single-thread UMMA issuer.  All warps run with the launch allocation of
 // 168 registers per thread.
 constexpr int kBwdThreads = 384;
@@ -224,6 +225,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
   if (threadIdx.x == 0 && smem_ok) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmdO);
     mbar_init(BAR(DQ_OUTER), 1);
     for (int s = 0; s < 4; ++s) {
       mbar_init(BAR(DQ_KFULL + s), 1);
@@ -419,21 +424,24 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 template <int D>
 struct DkdvCfg {
   static constexpr int kTile = kBT * D * 2;
-  static constexpr int kPT = kBT * kBT * 2;  // P^T buffer: 128 keys x 128 queries, 16-bit
-  static constexpr int kStat = 2 * kBT * 4;   // LSE and delta slices of one query tile
-  static constexpr int kBudget = kSmemOptin - 768 - 256;
-  static constexpr int kStagesFit = (kBudget - 2 * kTile - kPT) / (2 * kTile + kStat);
-  static constexpr int kStages = kStagesFit > 4 ? 4 : kStagesFit;
-  static_assert(kStages >= 2, "need a double-buffered Q / dO ring");
-  static constexpr int kOffK = 0, kOffV = kTile, kOffPT = 2 * kTile;
-  static constexpr int kOffStages = kOffPT + kPT;  // stage st: Q, dO
-  static constexpr int kOffStats = kOffStages + kStages * 2 * kTile;
-  static constexpr int kUsed = kOffStats + kStages * kStat + 256;
+  static constexpr int kStat = kBT * 4;  // one LSE (or delta) slice of a query tile
+  static constexpr int kBudget = kSmemOptin - 256;
+  static constexpr int kDOStages = 2;    // dO is released early (after dV), two stages suffice
+  static constexpr int kQFit = (kBudget - 2 * kTile - kDOStages * (kTile + kStat)) / (kTile + kStat);
+  static constexpr int kQStages = kQFit > 4 ? 4 : kQFit;  // Q is held until dK, so it gets more
+  static_assert(kQStages >= 3, "need a triple-buffered Q ring");
+  static constexpr int kOffK = 0, kOffV = kTile, kOffQ = 2 * kTile;
+  static constexpr int kOffDO = kOffQ + kQStages * kTile;
+  static constexpr int kOffLse = kOffDO + kDOStages * kTile;
+  static constexpr int kOffDelta = kOffLse + kQStages * kStat;
+  static constexpr int kUsed = kOffDelta + kDOStages * kStat + 256;
+  static_assert(kUsed <= kSmemOptin, "shared memory budget");
 };
 
 enum : int {
-  KV_OUTER = 0, KV_SFULL = 1 /* + stage */, KV_SEMPTY = 5 /* + stage */, KV_STFULL = 9, KV_STFREE = 10,
-  KV_PREADY = 11, KV_PTFREE = 12, KV_DPFULL = 13, KV_DSREADY = 14, KV_ACC = 15, KV_DRAIN = 16
+  KV_OUTER = 0, KV_QFULL = 1 /* + Q stage (4) */, KV_QEMPTY = 5 /* + Q stage (4) */,
+  KV_OFULL = 9 /* + dO stage (2) */, KV_OEMPTY = 11 /* + dO stage (2) */, KV_STFULL = 13,
+  KV_PREADY = 14, KV_DPFULL = 15, KV_DSREADY = 16, KV_ACC = 17, KV_DRAIN = 18
 };
 
 template <int D, bool BF16>
@@ -442,23 +450,30 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                     const BwdParams p) {
   using C = DkdvCfg<D>;
-  constexpr int ST = C::kStages;
+  constexpr int QST = C::kQStages, OST = C::kDOStages;
   bool smem_ok;
   const BwdSmem sm = bwd_smem<C::kUsed>(smem_ok);
 #define BAR(i) (sm.bar0 + 8u * static_cast<uint32_t>(i))
-  const uint32_t sK = sm.base + C::kOffK, sV = sm.base + C::kOffV, sPT = sm.base + C::kOffPT;
+  const uint32_t sK = sm.base + C::kOffK, sV = sm.base + C::kOffV;
+  const uint32_t sQ = sm.base + C::kOffQ, sdO = sm.base + C::kOffDO;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
   if (threadIdx.x == 0 && smem_ok) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmdO);
     mbar_init(BAR(KV_OUTER), 1);
     for (int s = 0; s < 4; ++s) {
-      mbar_init(BAR(KV_SFULL + s), 1);
-      mbar_init(BAR(KV_SEMPTY + s), 1);
+      mbar_init(BAR(KV_QFULL + s), 1);
+      mbar_init(BAR(KV_QEMPTY + s), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(BAR(KV_OFULL + s), 1);
+      mbar_init(BAR(KV_OEMPTY + s), 1);
     }
     mbar_init(BAR(KV_STFULL), 1);
-    mbar_init(BAR(KV_STFREE), 256);
     mbar_init(BAR(KV_PREADY), 256);
-    mbar_init(BAR(KV_PTFREE), 1);
     mbar_init(BAR(KV_DPFULL), 1);
     mbar_init(BAR(KV_DSREADY), 256);
     mbar_init(BAR(KV_ACC), 1);
@@ -483,7 +498,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (warp >= 8) {
     if (warp == kBwdWarpLoadA) {
-      // ---------------- TMA: K and V once, then Q / dO tiles with their LSE / delta slices
+      // ---------------- TMA: K and V once, then the Q tiles with their LSE slices
       if (lane == 0) {
         const uint64_t pol_once = policy_evict_first();
         const uint64_t pol_shared = policy_evict_last();
@@ -494,38 +509,58 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         int issued = 0;
         for (int s = 0; s < nsteps; ++s) {
-          const int st = s % ST;
-          if (!mbar_wait(BAR(KV_SEMPTY + st), ((s / ST) & 1) ^ 1, p.status, kDevTimeoutBwd)) break;
+          const int st = s % QST;
+          if (!mbar_wait(BAR(KV_QEMPTY + st), ((s / QST) & 1) ^ 1, p.status, kDevTimeoutBwd)) break;
           const int hh = s / nqi, it = j + (s - hh * nqi);
           const int bh = b * p.H + g * p.group + hh;
-          const uint32_t sQs = sm.base + C::kOffStages + st * 2 * C::kTile;
-          const uint32_t stat = sm.base + C::kOffStats + st * C::kStat;
           const int rows = min(kBT, p.S - it * kBT);  // a multiple of 64 (S % 64 == 0)
-          mbar_arrive_expect_tx(BAR(KV_SFULL + st), 2 * C::kTile + 2 * rows * 4);
-          for (int c = 0; c < D / 64; ++c) {
-            tma_load_3d(sQs + c * (kBT * 128), &tmQ, BAR(KV_SFULL + st), c * 64, it * kBT, bh, pol_shared);
-            tma_load_3d(sQs + C::kTile + c * (kBT * 128), &tmdO, BAR(KV_SFULL + st), c * 64, it * kBT, bh, pol_shared);
-          }
-          const size_t row0 = static_cast<size_t>(bh) * p.S + static_cast<size_t>(it) * kBT;
-          bulk_load(stat, p.lse + row0, rows * 4, BAR(KV_SFULL + st));
-          bulk_load(stat + kBT * 4, p.delta + row0, rows * 4, BAR(KV_SFULL + st));
+          mbar_arrive_expect_tx(BAR(KV_QFULL + st), C::kTile + rows * 4);
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_3d(sQ + st * C::kTile + c * (kBT * 128), &tmQ, BAR(KV_QFULL + st), c * 64, it * kBT, bh,
+                        pol_shared);
+          bulk_load(sm.base + C::kOffLse + st * C::kStat, p.lse + static_cast<size_t>(bh) * p.S + it * kBT,
+                    rows * 4, BAR(KV_QFULL + st));
           ++issued;
         }
         drain_wait(BAR(KV_OUTER), 0, p.status);
-        for (int s = max(0, issued - ST); s < issued; ++s) drain_wait(BAR(KV_SFULL + s % ST), (s / ST) & 1, p.status);
+        for (int s = max(0, issued - QST); s < issued; ++s) drain_wait(BAR(KV_QFULL + s % QST), (s / QST) & 1, p.status);
+      }
+      __syncwarp();
+    } else if (warp == kBwdWarpLoadB) {
+      // ---------------- TMA: the dO tiles with their delta slices
+      if (lane == 0) {
+        const uint64_t pol_shared = policy_evict_last();
+        int issued = 0;
+        for (int s = 0; s < nsteps; ++s) {
+          const int st = s % OST;
+          if (!mbar_wait(BAR(KV_OEMPTY + st), ((s / OST) & 1) ^ 1, p.status, kDevTimeoutBwd)) break;
+          const int hh = s / nqi, it = j + (s - hh * nqi);
+          const int bh = b * p.H + g * p.group + hh;
+          const int rows = min(kBT, p.S - it * kBT);
+          mbar_arrive_expect_tx(BAR(KV_OFULL + st), C::kTile + rows * 4);
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_3d(sdO + st * C::kTile + c * (kBT * 128), &tmdO, BAR(KV_OFULL + st), c * 64, it * kBT, bh,
+                        pol_shared);
+          bulk_load(sm.base + C::kOffDelta + st * C::kStat, p.delta + static_cast<size_t>(bh) * p.S + it * kBT,
+                    rows * 4, BAR(KV_OFULL + st));
+          ++issued;
+        }
+        for (int s = max(0, issued - OST); s < issued; ++s) drain_wait(BAR(KV_OFULL + s % OST), (s / OST) & 1, p.status);
       }
       __syncwarp();
     } else if (warp == kBwdWarpMma) {
-      // ---------------- UMMA issuer
+      // ---------------- UMMA issuer.  Per step s: dV += P^T(s) dO(s) (P^T read from TMEM where it
+      // overwrote S^T(s)), then S^T(s+1) into the same columns, dK += dS^T(s) Q(s) (dS^T over
+      // dP^T(s)), then dP^T(s+1).  Each barrier's next phase needs its waiter to have passed the
+      // current one (S^T(s+1) follows PREADY(s), dP^T(s+1) follows DSREADY(s)), so no barrier can
+      // run two phases ahead of the parity waited on.
       if (lane == 0) {
         const uint64_t dKd = sdesc_sw128(sK, 16, 1024), dVd = sdesc_sw128(sV, 16, 1024);
-        const uint64_t dPTd = sdesc_sw128(sPT, 16, 1024);
-        const uint32_t s0 = sm.base + C::kOffStages;
-        const uint64_t dQk = sdesc_sw128(s0, 16, 1024), dOk = sdesc_sw128(s0 + C::kTile, 16, 1024);
-        const uint64_t dQm = sdesc_sw128(s0, kBT * 128, 1024), dOm = sdesc_sw128(s0 + C::kTile, kBT * 128, 1024);
-        constexpr uint32_t kStageStep = 2 * C::kTile;
+        const uint64_t dQk = sdesc_sw128(sQ, 16, 1024), dOk = sdesc_sw128(sdO, 16, 1024);
+        const uint64_t dQm = sdesc_sw128(sQ, kBT * 128, 1024), dOm = sdesc_sw128(sdO, kBT * 128, 1024);
         bool ok = mbar_wait(BAR(KV_OUTER), 0, p.status, kDevTimeoutBwd) &&
-                  mbar_wait(BAR(KV_SFULL + 0), 0, p.status, kDevTimeoutBwd);
+                  mbar_wait(BAR(KV_QFULL + 0), 0, p.status, kDevTimeoutBwd) &&
+                  mbar_wait(BAR(KV_OFULL + 0), 0, p.status, kDevTimeoutBwd);
         if (ok) {
           tc_fence_after();
           umma_rows_rows<D, BF16>(tST, dKd, dQk);  // S^T(0) = K Q_0^T
@@ -534,26 +569,27 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           umma_commit(BAR(KV_DPFULL));
         }
         for (int s = 0; ok && s < nsteps; ++s) {
-          const int st = s % ST;
-          const uint32_t so = st * kStageStep;
-          if (s + 1 < nsteps) {
-            const uint32_t so1 = ((s + 1) % ST) * kStageStep;
-            if (!(ok = mbar_wait(BAR(KV_STFREE), s & 1, p.status, kDevTimeoutBwd))) break;
-            if (!(ok = mbar_wait(BAR(KV_SFULL + (s + 1) % ST), ((s + 1) / ST) & 1, p.status, kDevTimeoutBwd))) break;
-            tc_fence_after();
-            umma_rows_rows<D, BF16>(tST, dKd, desc_add(dQk, so1));
-            umma_commit(BAR(KV_STFULL));
-          }
+          const int qs = s % QST, os = s % OST;
           if (!(ok = mbar_wait(BAR(KV_PREADY), s & 1, p.status, kDevTimeoutBwd))) break;
           tc_fence_after();
-          umma_smem_tile<D, BF16>(tDV, dPTd, desc_add(dOm, so), s > 0 ? 1u : 0u);  // dV += P^T dO
-          umma_commit(BAR(KV_PTFREE));
+          umma_tmem_tile<D, BF16>(tDV, tST, desc_add(dOm, os * C::kTile), s > 0 ? 1u : 0u);  // dV += P^T dO
+          umma_commit(BAR(KV_OEMPTY + os));  // dO(s): read by dP^T(s) and dV(s)
+          if (s + 1 < nsteps) {
+            const int q1 = (s + 1) % QST;
+            if (!(ok = mbar_wait(BAR(KV_QFULL + q1), ((s + 1) / QST) & 1, p.status, kDevTimeoutBwd))) break;
+            tc_fence_after();
+            umma_rows_rows<D, BF16>(tST, dKd, desc_add(dQk, q1 * C::kTile));  // S^T(s+1)
+            umma_commit(BAR(KV_STFULL));
+          }
           if (!(ok = mbar_wait(BAR(KV_DSREADY), s & 1, p.status, kDevTimeoutBwd))) break;
           tc_fence_after();
-          umma_tmem_tile<D, BF16>(tDK, tDPT, desc_add(dQm, so), s > 0 ? 1u : 0u);  // dK += dS^T Q
-          umma_commit(BAR(KV_SEMPTY + st));
+          umma_tmem_tile<D, BF16>(tDK, tDPT, desc_add(dQm, qs * C::kTile), s > 0 ? 1u : 0u);  // dK += dS^T Q
+          umma_commit(BAR(KV_QEMPTY + qs));  // Q(s): read by S^T(s) and dK(s)
           if (s + 1 < nsteps) {
-            umma_rows_rows<D, BF16>(tDPT, dVd, desc_add(dOk, ((s + 1) % ST) * kStageStep));
+            const int o1 = (s + 1) % OST;
+            if (!(ok = mbar_wait(BAR(KV_OFULL + o1), ((s + 1) / OST) & 1, p.status, kDevTimeoutBwd))) break;
+            tc_fence_after();
+            umma_rows_rows<D, BF16>(tDPT, dVd, desc_add(dOk, o1 * C::kTile));  // dP^T(s+1)
             umma_commit(BAR(KV_DPFULL));
           }
         }
@@ -570,10 +606,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int key = j * kBT + row;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const float scale = p.scale_log2;
-    uint8_t* const pt_row = sm.ptr + C::kOffPT + w * (kBT * 128) + row * 128;
     bool ok = true;
     for (int s = 0; s < nsteps; ++s) {
-      const int st = s % ST;
+      const int qs = s % QST, os = s % OST;
       const int hh = s / nqi, it = j + (s - hh * nqi);
       if (!(ok = warp_all(mbar_wait(BAR(KV_STFULL), s & 1, p.status, kDevTimeoutBwd)))) break;
       tc_fence_after();
@@ -582,10 +617,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tmem_ld32(tST + lane_off + 64 * w + 32, sv[1]);
       tmem_ld_wait(sv[0]);
       tmem_ld_wait(sv[1]);
-      tc_fence_before();
-      mbar_arrive(BAR(KV_STFREE));
-      const float* lse = reinterpret_cast<const float*>(sm.ptr + C::kOffStats + st * C::kStat) + 64 * w;
-      const float* del = lse + kBT;
+      const float* lse = reinterpret_cast<const float*>(sm.ptr + C::kOffLse + qs * C::kStat) + 64 * w;
+      const float* del = reinterpret_cast<const float*>(sm.ptr + C::kOffDelta + os * C::kStat) + 64 * w;
       float neg_lse[64];
 #pragma unroll
       for (int c = 0; c < 64; c += 4) {
@@ -604,17 +637,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int c = 0; c < 64; ++c)
           if (key > q0 + c || q0 + c >= p.S) pr[c] = 0.f;
       }
-      // P^T -> shared memory (row = key, 128-byte swizzle), once dV of the previous step is done
-      if (s > 0 && !(ok = warp_all(mbar_wait(BAR(KV_PTFREE), (s - 1) & 1, p.status, kDevTimeoutBwd)))) break;
+      // P^T -> TMEM over the first half of this warpgroup's own S^T columns (already read)
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const uint4 v = make_uint4(pack2<BF16>(pr[8 * u], pr[8 * u + 1]), pack2<BF16>(pr[8 * u + 2], pr[8 * u + 3]),
-                                   pack2<BF16>(pr[8 * u + 4], pr[8 * u + 5]), pack2<BF16>(pr[8 * u + 6], pr[8 * u + 7]));
-        *reinterpret_cast<uint4*>(pt_row + ((u ^ (row & 7)) << 4)) = v;
+      for (int h2 = 0; h2 < 2; ++h2) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = pack2<BF16>(pr[32 * h2 + 2 * i], pr[32 * h2 + 2 * i + 1]);
+        tmem_st16(tST + lane_off + 64 * w + 16 * h2, pk);
       }
-      fence_async_shared();
+      tmem_st_wait();
+      tc_fence_before();
       mbar_arrive(BAR(KV_PREADY));
-      // dS^T = P^T (dP^T - delta) -> TMEM over dP^T
+      // dS^T = P^T (dP^T - delta) -> TMEM over dP^T.  On a ragged last query tile the delta
+      // slice past S holds stale bytes: those queries (P = 0) read delta as 0, never 0 * NaN.
+      const bool ragged = q0 + 64 > p.S;
       if (!(ok = warp_all(mbar_wait(BAR(KV_DPFULL), s & 1, p.status, kDevTimeoutBwd)))) break;
       tc_fence_after();
       uint32_t dp[2][32];
@@ -627,8 +663,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int c4 = 0; c4 < 8; ++c4) {
-          const float4 d4 = *reinterpret_cast<const float4*>(del + 32 * h2 + 4 * c4);
           const int c = 32 * h2 + 4 * c4;
+          float4 d4 = *reinterpret_cast<const float4*>(del + c);
+          if (ragged) {
+            d4.x = q0 + c < p.S ? d4.x : 0.f;
+            d4.y = q0 + c + 1 < p.S ? d4.y : 0.f;
+            d4.z = q0 + c + 2 < p.S ? d4.z : 0.f;
+            d4.w = q0 + c + 3 < p.S ? d4.w : 0.f;
+          }
           const uint64_t a = fmul2(f2(pr[c], pr[c + 1]),
                                    fadd2(f2u(dp[h2][4 * c4], dp[h2][4 * c4 + 1]), f2(-d4.x, -d4.y)));
           const uint64_t bb = fmul2(f2(pr[c + 2], pr[c + 3]),

@@ -41,9 +41,16 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only if the 
 
 template <int D, int BN>
 struct FwdCfg {
-  static constexpr int kChunks = D / 64;            // 64-column (128-byte) swizzle chunks
-  static constexpr int kQChunkBytes = kBM * 128;
-  static constexpr int kKVChunkBytes = BN * 128;
+  // Shared-memory tiles are rows of swizzle chunks: 64 columns (128-byte rows, 128-byte swizzle)
+  // for D = 64 and 128, one 32-column chunk (64-byte rows, 64-byte swizzle) for D = 32.
+  static constexpr int kSwBytes = D >= 64 ? 128 : 64;
+  static constexpr int kChunkCols = kSwBytes / 2;
+  static constexpr uint32_t kLayout = D >= 64 ? kLayoutSw128 : kLayoutSw64;
+  static constexpr int kSbo = 8 * kSwBytes;           // bytes between 8-row groups
+  static constexpr int kKStepsPerChunk = kSwBytes / 32;  // 16-element UMMA K steps per row
+  static constexpr int kChunks = D / kChunkCols;
+  static constexpr int kQChunkBytes = kBM * kSwBytes;
+  static constexpr int kKVChunkBytes = BN * kSwBytes;
   static constexpr int kQBytes = kBM * D * 2;
   static constexpr int kKVBytes = BN * D * 2;       // one K (or V) tile
   static constexpr int kXchBytes = 2 * 2 * 2 * kBM * 4 + 2 * 2 * kBM * 4;  // row-max (x2 parity) + row-sum
@@ -146,10 +153,11 @@ template <int D, int BN, bool BF16>
 __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint64_t q_desc, uint64_t k_desc) {
   using C = FwdCfg<D, BN>;
   constexpr uint32_t IDESC = idesc_f16(BF16, kBM, BN, false, false);  // Q, K both K-major
+  constexpr int KS = C::kKStepsPerChunk;
 #pragma unroll
   for (int k = 0; k < D / 16; ++k) {
-    umma_ss(d_tmem, desc_add(q_desc, (k / 4) * C::kQChunkBytes + (k % 4) * 32),
-            desc_add(k_desc, (k / 4) * C::kKVChunkBytes + (k % 4) * 32), IDESC, k > 0 ? 1u : 0u);
+    umma_ss(d_tmem, desc_add(q_desc, (k / KS) * C::kQChunkBytes + (k % KS) * 32),
+            desc_add(k_desc, (k / KS) * C::kKVChunkBytes + (k % KS) * 32), IDESC, k > 0 ? 1u : 0u);
   }
 }
 
@@ -162,10 +170,11 @@ __device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint6
                                          uint32_t accumulate) {
   constexpr uint32_t IDESC = idesc_f16(BF16, kBM, D, false, true);
   constexpr int kStepsPerHalf = BN / 32;
+  constexpr int kKeyStep = 16 * FwdCfg<D, BN>::kSwBytes;  // 16 key rows of V
 #pragma unroll
   for (int k = 0; k < BN / 16; ++k)
     umma_ts(o_tmem, p_tmem + (k / kStepsPerHalf) * (BN / 2) + (k % kStepsPerHalf) * 8,
-            desc_add(v_desc, k * 2048), IDESC, (accumulate | k) ? 1u : 0u);
+            desc_add(v_desc, k * kKeyStep), IDESC, (accumulate | k) ? 1u : 0u);
 }
 
 template <int D, int BN, bool BF16>
@@ -237,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive_expect_tx(BAR(BAR_Q), w.ntiles * C::kQBytes);
       for (int t = 0; t < w.ntiles; ++t)
         for (int c = 0; c < C::kChunks; ++c)
-          tma_load_3d(sQ + t * C::kQBytes + c * C::kQChunkBytes, &tmQ, BAR(BAR_Q), c * 64,
+          tma_load_3d(sQ + t * C::kQBytes + c * C::kQChunkBytes, &tmQ, BAR(BAR_Q), c * C::kChunkCols,
                       w.t[t].qt * kBM, w.t[t].bh, pol_q);
       int issued = 0;
       for (int j = 0; j < nmax; ++j) {
@@ -245,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(BAR(BAR_KEMPTY + s), ((j / KST) & 1) ^ 1, p.status, kDevTimeoutKVEmpty)) break;
         mbar_arrive_expect_tx(BAR(BAR_KFULL + s), C::kKVBytes);
         for (int c = 0; c < C::kChunks; ++c)
-          tma_load_3d(sK + s * C::kKVBytes + c * C::kKVChunkBytes, &tmK, BAR(BAR_KFULL + s), c * 64,
+          tma_load_3d(sK + s * C::kKVBytes + c * C::kKVChunkBytes, &tmK, BAR(BAR_KFULL + s), c * C::kChunkCols,
                       j * BN, w.bh_kv, pol_kv);
         ++issued;
       }
@@ -265,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(BAR(BAR_VEMPTY + s), ((j / VST) & 1) ^ 1, p.status, kDevTimeoutKVEmpty)) break;
         mbar_arrive_expect_tx(BAR(BAR_VFULL + s), C::kKVBytes);
         for (int c = 0; c < C::kChunks; ++c)
-          tma_load_3d(sV + s * C::kKVBytes + c * C::kKVChunkBytes, &tmV, BAR(BAR_VFULL + s), c * 64,
+          tma_load_3d(sV + s * C::kKVBytes + c * C::kKVChunkBytes, &tmV, BAR(BAR_VFULL + s), c * C::kChunkCols,
                       j * BN, w.bh_kv, pol_kv);
         ++issued;
       }
@@ -276,10 +285,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ UMMA issuer (one thread)
     if (lane == 0) {
-      const uint64_t dq0 = sdesc_sw128(sQ, 16, 1024);
-      const uint64_t dq1 = sdesc_sw128(sQ + C::kQBytes, 16, 1024);
-      const uint64_t dk0 = sdesc_sw128(sK, 16, 1024);
-      const uint64_t dv0 = sdesc_sw128(sV, C::kKVChunkBytes, 1024);
+      const uint64_t dq0 = sdesc_sw(sQ, 16, C::kSbo, C::kLayout);
+      const uint64_t dq1 = sdesc_sw(sQ + C::kQBytes, 16, C::kSbo, C::kLayout);
+      const uint64_t dk0 = sdesc_sw(sK, 16, C::kSbo, C::kLayout);
+      const uint64_t dv0 = sdesc_sw(sV, C::kKVChunkBytes, C::kSbo, C::kLayout);
       const uint32_t tS0 = tmem, tS1 = tmem + 128, tO0 = tmem + 256, tO1 = tmem + 384;
       const int n0 = w.nkv[0], n1 = w.nkv[1];
       bool ok = mbar_wait(BAR(BAR_Q), 0, p.status, kDevTimeoutQ) &&
@@ -441,14 +450,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Rescale this half of the running O if any row's max moved (P V of tile j-1 is complete:
         // it was issued before S_t(j), whose completion we waited for).
         if (j > 0 && __any_sync(0xffffffffu, upd)) {
+          if constexpr (D >= 64) {
 #pragma unroll 1
-          for (int c = 0; c < D / 64; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tO + c * 32, o);
-            tmem_ld_wait(o);
+            for (int c = 0; c < D / 64; ++c) {
+              uint32_t o[32];
+              tmem_ld32(tO + c * 32, o);
+              tmem_ld_wait(o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(tO + c * 32, o);
+              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+              tmem_st32(tO + c * 32, o);
+            }
+          } else {  // D = 32: 16 columns per half
+            uint32_t o[16];
+            tmem_ld16(tO, o);
+            tmem_ld_wait16(o);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st16(tO, o);
           }
         }
         tmem_st_wait();
@@ -467,21 +485,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float inv_l = 1.0f / l_row;
         uint8_t* orow = reinterpret_cast<uint8_t*>(p.o) +
                         (static_cast<size_t>(tile.bh) * p.S + qrow) * (D * 2) + h * D;
+        if constexpr (D >= 64) {
 #pragma unroll 1
-        for (int c = 0; c < D / 64; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + c * 32, o);
-          tmem_ld_wait(o);
-          uint32_t pk[16];
+          for (int c = 0; c < D / 64; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_ld_wait(o);
+            uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            pk[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l,
-                                __uint_as_float(o[2 * i + 1]) * inv_l);
+            for (int i = 0; i < 16; ++i)
+              pk[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l,
+                                  __uint_as_float(o[2 * i + 1]) * inv_l);
+            if (qrow < p.S) {
+              uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+#pragma unroll
+              for (int v = 0; v < 4; ++v)
+                dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+            }
+          }
+        } else {  // D = 32: 16 columns (32 bytes) per half
+          uint32_t o[16];
+          tmem_ld16(tO, o);
+          tmem_ld_wait16(o);
+          uint32_t pk[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            pk[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
           if (qrow < p.S) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
-#pragma unroll
-            for (int v = 0; v < 4; ++v)
-              dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+            uint4* dst = reinterpret_cast<uint4*>(orow);
+            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
           }
         }
         if (h == 0 && p.lse != nullptr && qrow < p.S)
@@ -517,10 +550,14 @@ cudaError_t launch_fwd(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUt
 #define FA_FWD_CASE(DD, NN, BB)                                              \
   if (D == DD && block_n == NN && bf16 == BB)                                \
     return launch_fwd_t<DD, NN, BB>(tmQ, tmK, tmV, p, stream);
+  FA_FWD_CASE(32, 64, false)
+  FA_FWD_CASE(32, 128, false)
   FA_FWD_CASE(64, 64, false)
   FA_FWD_CASE(64, 128, false)
   FA_FWD_CASE(128, 64, false)
   FA_FWD_CASE(128, 128, false)
+  FA_FWD_CASE(32, 64, true)
+  FA_FWD_CASE(32, 128, true)
   FA_FWD_CASE(64, 64, true)
   FA_FWD_CASE(64, 128, true)
   FA_FWD_CASE(128, 64, true)

@@ -224,14 +224,22 @@ __device__ __forceinline__ void tc_fence_after() {
 // K-major SW128 (rows of 128 B, 8-row atoms of 1 KiB): SBO = 1024, LBO unused.
 // MN-major SW128: LBO = byte distance between 64-element MN chunks, SBO = byte distance
 // between 8-row K groups (1024 for densely stacked rows).
-__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+// Swizzle-mode codes of the descriptor's [61,64) field.
+constexpr uint32_t kLayoutSw128 = 2;  // 128-byte rows, 8-row (1 KiB) atoms
+constexpr uint32_t kLayoutSw64 = 4;   // 64-byte rows, 8-row (512 B) atoms
+
+__device__ __forceinline__ uint64_t sdesc_sw(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
   d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
   d |= static_cast<uint64_t>(1) << 46;
-  d |= static_cast<uint64_t>(2) << 61;
+  d |= static_cast<uint64_t>(layout) << 61;
   return d;
+}
+
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return sdesc_sw(saddr, lbo, sbo, kLayoutSw128);
 }
 
 // Advance a descriptor's start address by `bytes` (a multiple of 16).  The start-address field

@@ -3,7 +3,7 @@
     python run_attention.py --input INPUT.npz --output OUTPUT.npy --backend cutile
 
 Input:  .npz with contiguous float16 arrays Q, K, V, each [B, H, N, D];
-        1<=B<=16, 1<=H<=32, 1<=N<=32768, D in {64, 128}, N divisible by --block-m and --block-n
+        1<=B<=16, 1<=H<=32, 1<=N<=32768, D in {32, 64, 128}, N divisible by --block-m and --block-n
 Output: .npy, float16, shape [B, H, N, D]
 Backends: cutile / fused (sm_100a kernel), unfused (not built on B200), reference (PyTorch fp32)
 Exit status: 0 success, 2 unsupported input or usage error, 1 runtime failure.

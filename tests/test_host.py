@@ -59,10 +59,21 @@ def _fwd_rc(**kw):
 
 @pytest.mark.parametrize("kw,code", [
     (dict(B=0), 1), (dict(S=0), 1), (dict(H=6, H_kv=4), 1), (dict(q=0), 1), (dict(st=0), 1),
-    (dict(D=32), 2), (dict(D=96), 2), (dict(dtype=2), 2), (dict(tm=32), 2), (dict(tn=256), 2),
+    (dict(D=48), 2), (dict(D=96), 2), (dict(dtype=2), 2), (dict(tm=32), 2), (dict(tn=256), 2),
 ])
 def test_c_abi_rejects_bad_arguments_before_touching_the_device(kw, code):
     assert _fwd_rc(**kw) == code
+
+
+def test_backward_rejects_head_dim_32_before_touching_the_device():
+    """D = 32 is a forward head dim only: every backward entry point answers FA_ERR_UNSUPPORTED."""
+    lib = _native().load()
+    vp = ctypes.c_void_p
+    p = vp(16)
+    assert lib.fa_bwd_preprocess(p, p, p, 1, 8, 128, 32, 0, p, None) == 2
+    assert lib.fa_bwd_dkdv(p, p, p, p, p, p, p, p, 1, 8, 8, 128, 32, 0, 64, 64, p, None) == 2
+    assert lib.fa_bwd_dq(p, p, p, p, p, p, p, 1, 8, 8, 128, 32, 0, 64, 64, p, None) == 2
+    assert lib.fa_bwd_noalloc(p, p, p, p, p, p, p, p, p, 1, 8, 8, 128, 32, 0, 64, 64, p, None) == 2
 
 
 def test_python_wrappers_keep_reference_errors():
@@ -89,8 +100,10 @@ def test_validation_contract():
     validate_qkv(ok, ok, ok, 64, 64)
     with pytest.raises(ValidationError, match="only float16 and bfloat16"):
         validate_qkv(ok.astype(np.float32), ok, ok, 64, 64)
-    with pytest.raises(ValidationError, match="head dim D=32"):
-        z = np.zeros((1, 1, 128, 32), np.float16)
+    z = np.zeros((1, 1, 128, 32), np.float16)
+    validate_qkv(z, z, z, 64, 64)  # D = 32 is a reference head dim
+    with pytest.raises(ValidationError, match="head dim D=96"):
+        z = np.zeros((1, 1, 128, 96), np.float16)
         validate_qkv(z, z, z, 64, 64)
     with pytest.raises(ValidationError, match="not divisible"):
         validate_qkv(ok, ok, ok, 128, 48)
