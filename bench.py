@@ -12,7 +12,8 @@ attention.dist.sharded_attention_autograd, which all-gathers O and dQ/dK/dV over
 
 value  = fwd+bwd causal TFLOP/s of the whole job (3.5 * 2 * B * H * S^2 * D per step, the
          reference's convention), device time, max over ranks, inputs resident in HBM.
-e2e    = the same metric with pinned-host inputs copied in and O/dQ/dK/dV copied out every step.
+e2e    = the same metric with pinned-host inputs copied in and O/dQ/dK/dV copied out every step
+         (batch slices pipelined: copy-in, compute and copy-out of different slices overlap).
 roofline: the dominant kernel, timed alone with CUDA events on its launch stream.
 cpu_baseline: the reference's PyTorch fp32 path on the host cores, on a bounded sample.
 --impl reference: the reference's CPU implementation (oracle port) timed the same way.
@@ -327,17 +328,50 @@ def main():
     hdk = torch.empty(k.shape, dtype=dt).pin_memory()
     hdv = torch.empty(v.shape, dtype=dt).pin_memory()
 
+    # The host-resident job streams through the public API one batch slice at a time (attention
+    # is independent per batch entry): slice c+1 copies in on one stream while slice c computes
+    # and slice c-1 copies out on another (PCIe is full duplex).  Every byte of Q, K, V, dO goes
+    # in and every byte of O, dQ, dK, dV comes out inside the timed region.  A slice is `world`
+    # batch entries, so with N GPUs each rank still gets a full share of every call; on one GPU
+    # with MHA each batch entry is cut into two head halves (contiguous, independent), which
+    # halves the copy-in of the first slice and the copy-out of the last, the parts no compute
+    # can hide.
+    h2d_stream = torch.cuda.Stream(device=dev)
+    d2h_stream = torch.cuda.Stream(device=dev)
+    comp = torch.cuda.current_stream(dev)
+    bs = world
+    hsplit = 2 if (world == 1 and H_kv == H and H % 2 == 0) else 1
+    hh = H // hsplit
+    slices = [(slice(c * bs, (c + 1) * bs), slice(p * hh, (p + 1) * hh))
+              for c in range(B // bs) for p in range(hsplit)]
+    nslices = len(slices)
+
     def e2e_step():
-        dq_ = hq.to(dev, non_blocking=True).requires_grad_(True)
-        dk_ = hk.to(dev, non_blocking=True).requires_grad_(True)
-        dv_ = hv.to(dev, non_blocking=True).requires_grad_(True)
-        ddo = hdo.to(dev, non_blocking=True)
-        o = attn(dq_, dk_, dv_)
-        o.backward(ddo)
-        ho.copy_(o.detach(), non_blocking=True)
-        hdq.copy_(dq_.grad, non_blocking=True)
-        hdk.copy_(dk_.grad, non_blocking=True)
-        hdv.copy_(dv_.grad, non_blocking=True)
+        h2d_stream.wait_stream(comp)
+        ins = []
+        for sb, sh in slices:
+            sl = (sb, sh) if hsplit > 1 else (sb,)
+            with torch.cuda.stream(h2d_stream):
+                tens = [t[sl].to(dev, non_blocking=True) for t in (hq, hk, hv, hdo)]
+                ready = torch.cuda.Event()
+                ready.record(h2d_stream)
+            ins.append((sl, tens, ready))
+        keep = []
+        for sl, (tq, tk, tv, tdo), ready in ins:
+            comp.wait_event(ready)
+            q_, k_, v_ = (t.requires_grad_(True) for t in (tq, tk, tv))
+            o = attn(q_, k_, v_)
+            o.backward(tdo)
+            done = torch.cuda.Event()
+            done.record(comp)
+            with torch.cuda.stream(d2h_stream):
+                d2h_stream.wait_event(done)
+                ho[sl].copy_(o.detach(), non_blocking=True)
+                hdq[sl].copy_(q_.grad, non_blocking=True)
+                hdk[sl].copy_(k_.grad, non_blocking=True)
+                hdv[sl].copy_(v_.grad, non_blocking=True)
+            keep.append((tq, tk, tv, tdo, o))  # no buffer is reused before the copies end
+        comp.wait_stream(d2h_stream)
 
     e2e_step()
     ms_e2e = timed(e2e_step, a.e2e_steps)
@@ -345,6 +379,7 @@ def main():
     d2h = sum(t.numel() * t.element_size() for t in (ho, hdq, hdk, hdv))
     e2e = {"value": flops_step * a.e2e_steps / (ms_e2e / 1e3) / 1e12, "unit": UNIT,
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": a.e2e_steps,
+           "slices_per_step": nslices,
            "ms_per_step": ms_e2e / a.e2e_steps}
 
     cpu = None
