@@ -141,6 +141,7 @@ int fa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int
                                       : static_cast<long long>(B) * (H / 2) * p.nq;
   if (items > 0x7fffffffLL) return FA_ERR_UNSUPPORTED;
   p.n_items = static_cast<int>(items);
+  p.band = fa::work_band(p.mode == 0 ? static_cast<long long>(B) * H : static_cast<long long>(B) * (H / 2));
   p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
   cudaError_t e = fa::launch_fwd(tmQ, tmK, tmV, p, D, tile_n, dtype == FA_DTYPE_BF16,
                                  static_cast<cudaStream_t>(stream));
@@ -219,6 +220,7 @@ int fa_bwd_dkdv(const void* q, const void* k, const void* v, const void* dO, con
   if (rc != FA_OK) return rc;
   p.dk = dk;
   p.dv = dv;
+  p.band = fa::work_band(static_cast<long long>(B) * H_kv);
   cudaError_t e = fa::launch_bwd_dkdv(tmQ, tmK, tmV, tmdO, p, dtype == FA_DTYPE_BF16,
                                       static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? FA_OK : cuda_fail(e);
@@ -235,6 +237,7 @@ int fa_bwd_dq(const void* q, const void* k, const void* v, const void* dO, const
                        dev_status, &tmQ, &tmK, &tmV, &tmdO, &p, /*q_rows=*/128, /*kv_rows=*/128);
   if (rc != FA_OK) return rc;
   p.dq = dq;
+  p.band = fa::work_band(static_cast<long long>(B) * H);
   cudaError_t e = fa::launch_bwd_dq(tmQ, tmK, tmV, tmdO, p, dtype == FA_DTYPE_BF16,
                                     static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? FA_OK : cuda_fail(e);

@@ -253,10 +253,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_after();
   tmem = *sm.tmem_slot;
 
-  // work item: head major, query tile descending (the longest rows first)
+  // work item: bands of heads, query tile descending (the longest rows first)
   const int nqt = (p.S + kBT - 1) / kBT;
-  const int bh = blockIdx.x / nqt;
-  const int i = nqt - 1 - (blockIdx.x - bh * nqt);
+  const UnitLevel ul = band_order(blockIdx.x, p.B * p.H, nqt, p.band);
+  const int bh = ul.unit;
+  const int i = nqt - 1 - ul.level;
   const int b = bh / p.H, h = bh - b * p.H;
   const int bkv = b * p.H_kv + h / p.group;
   const int nsteps = min(i * kBT + kBT - 1, p.S - 1) / kBT + 1;
@@ -487,10 +488,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_after();
   tmem = *sm.tmem_slot;
 
-  // work item: (b, kv head) major, key tile ascending (tile 0 sees every query: heaviest first)
+  // work item: bands of (b, kv head), key tile ascending (tile 0 sees every query: heaviest first)
   const int nkt = (p.S + kBT - 1) / kBT;
-  const int bkv = blockIdx.x / nkt;
-  const int j = blockIdx.x - bkv * nkt;
+  const UnitLevel ul = band_order(blockIdx.x, p.B * p.H_kv, nkt, p.band);
+  const int bkv = ul.unit;
+  const int j = ul.level;
   const int b = bkv / p.H_kv, g = bkv - b * p.H_kv;
   const int nqi = nkt - j;  // query tiles j .. nkt-1 see these keys
   const int nsteps = p.group * nqi;

@@ -104,8 +104,9 @@ __device__ __forceinline__ Work decode_work(const FwdParams& p, int item) {
   Work w;
   if (p.mode == 0) {
     const int ncp = (p.nq + 1) / 2;
-    const int bh = item / ncp;
-    const int c = ncp - 1 - (item - bh * ncp);  // heavy (late) tile pairs of a head first
+    const UnitLevel ul = band_order(item, p.B * p.H, ncp, p.band);
+    const int bh = ul.unit;
+    const int c = ncp - 1 - ul.level;  // heavy (late) tile pairs first
     w.t[0] = {bh, 2 * c};
     w.t[1] = {bh, 2 * c + 1};
     w.ntiles = (2 * c + 1 < p.nq) ? 2 : 1;
@@ -113,8 +114,9 @@ __device__ __forceinline__ Work decode_work(const FwdParams& p, int item) {
     w.bh_kv = b * p.H_kv + h / p.group;
   } else {
     const int pairs_per_b = p.H / 2;
-    const int pi = item / p.nq;
-    const int i = p.nq - 1 - (item - pi * p.nq);
+    const UnitLevel ul = band_order(item, p.B * pairs_per_b, p.nq, p.band);
+    const int pi = ul.unit;
+    const int i = p.nq - 1 - ul.level;
     const int b = pi / pairs_per_b, hp = pi - b * pairs_per_b;
     const int h = 2 * hp;
     w.t[0] = {b * p.H + h, i};

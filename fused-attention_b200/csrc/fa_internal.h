@@ -21,6 +21,7 @@ struct FwdParams {
   int nq;             // number of 128-row query tiles = ceil(S / 128)
   int mode;           // 0: a CTA takes q-tiles (2c, 2c+1) of one head; 1: q-tile i of heads (2p, 2p+1)
   int n_items;        // grid size
+  int band;           // work units (heads or head pairs) ordered heavy-first together
   float scale_log2;   // log2(e) / sqrt(D)
 };
 
@@ -39,9 +40,14 @@ struct BwdParams {
   int S, H, H_kv, group, B, D;
   int nq;             // ceil(S / 128)
   int n_items;
+  int band;           // work units (heads) ordered heavy-first together
   float scale_log2;   // log2(e) / sqrt(D)
   float sm_scale;     // 1 / sqrt(D)
 };
+
+// Work units (heads, head pairs) whose tiles are launched heavy-first together: up to 16 units,
+// about 64 MiB of K/V at S = 8192, D = 128, so the heads in flight keep their K/V in the 126 MB L2.
+inline int work_band(long long units) { return units < 16 ? static_cast<int>(units) : 16; }
 
 // Launchers implemented in the kernel translation units.  They return a cudaError_t.
 cudaError_t launch_fwd(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,

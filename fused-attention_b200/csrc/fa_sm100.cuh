@@ -242,6 +242,23 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, ui
   return sdesc_sw(saddr, lbo, sbo, kLayoutSw128);
 }
 
+// Grid order: work item -> (unit, level), level 0 the heaviest.  Units come in bands of `band`;
+// inside a band the items run level by level (every unit's heaviest tile first), and the bands
+// follow each other.  Each band therefore ends with its lightest tiles, so the grid's tail is
+// short CTAs, while only a band of units (and their K/V) is in flight at a time.
+struct UnitLevel {
+  int unit;
+  int level;
+};
+__device__ __forceinline__ UnitLevel band_order(int item, int units, int levels, int band) {
+  const int per_band = band * levels;
+  const int b = item / per_band;
+  const int first = b * band;
+  const int size = min(band, units - first);
+  const int r = item - b * per_band;
+  return {first + r % size, r / size};
+}
+
 // Advance a descriptor's start address by `bytes` (a multiple of 16).  The start-address field
 // is the low 14 bits of (address >> 4); shared-memory addresses stay below 256 KiB, so the add
 // never carries into the next field.
