@@ -99,7 +99,7 @@ const char* fa_strerror(int code) {
   switch (code) {
     case FA_OK: return "ok";
     case FA_ERR_INVALID_ARG: return "invalid argument (null pointer, non-positive size or H not divisible by H_kv)";
-    case FA_ERR_UNSUPPORTED: return "unsupported configuration (D must be 32, 64 or 128 in the forward and 64 or 128 in the backward, dtype f16/bf16, tiles 64/128)";
+    case FA_ERR_UNSUPPORTED: return "unsupported configuration (D must be 32, 64 or 128, dtype f16/bf16, tiles 64/128)";
     case FA_ERR_ALIGNMENT: return "tensor base address is not 16-byte aligned";
     case FA_ERR_CUDA: return "CUDA runtime error (see fa_last_cuda_error)";
     case FA_ERR_DRIVER: return "cuTensorMapEncodeTiled unavailable or rejected the tensor";
@@ -151,7 +151,6 @@ int fa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int
 int fa_bwd_preprocess(const void* o, const void* dO, float* delta, int B, int H, int S, int D,
                       int dtype, int* dev_status, void* stream) {
   if (!o || !dO || !delta) return FA_ERR_INVALID_ARG;
-  if (D == 32) return FA_ERR_UNSUPPORTED;  // the backward kernels take D = 64 or 128
   int rc = check_common(B, H, H, S, D, dtype, 128, 128, dev_status);
   if (rc != FA_OK) return rc;
   if (!aligned16(o) || !aligned16(dO) || (reinterpret_cast<uintptr_t>(delta) & 3u))
@@ -177,7 +176,6 @@ static int bwd_prepare(const void* q, const void* k, const void* v, const void* 
                        CUtensorMap* tmQ, CUtensorMap* tmK, CUtensorMap* tmV, CUtensorMap* tmdO,
                        fa::BwdParams* p, int q_rows, int kv_rows) {
   if (!q || !k || !v || !dO || !lse || !delta) return FA_ERR_INVALID_ARG;
-  if (D == 32) return FA_ERR_UNSUPPORTED;  // the backward kernels take D = 64 or 128
   int rc = check_common(B, H, H_kv, S, D, dtype, tile_m, tile_n, dev_status);
   if (rc != FA_OK) return rc;
   // The backward streams whole 64-row tiles (and their lse / delta slices).

@@ -106,18 +106,55 @@ __device__ __forceinline__ void store_row_chunk(uint8_t* dst, const uint32_t (&v
   for (int q = 0; q < 4; ++q) d[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
 }
 
-// D[128 x 128] (+)= A[128 x D] * B[128 x D]^T, both K-major SW128 tiles of 128 rows.
+// Shared-memory geometry of a 128-row tile of head dim D: rows of swizzle chunks, 64 columns
+// (128-byte rows, 128-byte swizzle) for D = 64 and 128, one 32-column chunk (64-byte rows,
+// 64-byte swizzle) for D = 32.
+template <int D>
+struct BwdTile {
+  static constexpr int kSwBytes = D >= 64 ? 128 : 64;
+  static constexpr int kChunkCols = kSwBytes / 2;
+  static constexpr int kChunks = D / kChunkCols;
+  static constexpr int kChunkBytes = kBT * kSwBytes;  // one chunk of all 128 rows
+  static constexpr uint32_t kLayout = D >= 64 ? kLayoutSw128 : kLayoutSw64;
+  static constexpr int kSbo = 8 * kSwBytes;           // bytes between 8-row groups
+  static constexpr int kKSteps = kSwBytes / 32;       // 16-element K steps per row
+  static constexpr int kRowStep = 16 * kSwBytes;      // 16 rows: one K step of an MN-major operand
+};
+
+// K-major descriptor of a tile (A or B operand whose K dimension is the head dim).
+template <int D>
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t saddr) {
+  return sdesc_sw(saddr, 16, BwdTile<D>::kSbo, BwdTile<D>::kLayout);
+}
+// MN-major descriptor of a tile (B operand whose N dimension is the head dim, K the 128 rows).
+template <int D>
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t saddr) {
+  return sdesc_sw(saddr, BwdTile<D>::kChunkBytes, BwdTile<D>::kSbo, BwdTile<D>::kLayout);
+}
+
+// Load a 128-row tile (all D columns) of head `bh`, rows [row0, row0 + 128), with TMA.
+template <int D>
+__device__ __forceinline__ void load_tile(uint32_t dst, const CUtensorMap* map, uint32_t bar, int row0, int bh,
+                                          uint64_t policy) {
+  using T = BwdTile<D>;
+#pragma unroll
+  for (int c = 0; c < T::kChunks; ++c)
+    tma_load_3d(dst + c * T::kChunkBytes, map, bar, c * T::kChunkCols, row0, bh, policy);
+}
+
+// D[128 x 128] (+)= A[128 x D] * B[128 x D]^T, both K-major tiles of 128 rows.
 template <int D, bool BF16>
 __device__ __forceinline__ void umma_rows_rows(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc) {
+  using T = BwdTile<D>;
   constexpr uint32_t IDESC = idesc_f16(BF16, kBT, kBT, false, false);
 #pragma unroll
   for (int k = 0; k < D / 16; ++k) {
-    const uint32_t off = (k / 4) * (kBT * 128) + (k % 4) * 32;
+    const uint32_t off = (k / T::kKSteps) * T::kChunkBytes + (k % T::kKSteps) * 32;
     umma_ss(d_tmem, desc_add(a_desc, off), desc_add(b_desc, off), IDESC, k > 0 ? 1u : 0u);
   }
 }
 
-// acc[128 x D] (+)= A[128 x 128] (16-bit in TMEM, K-major) * B[128 x D] (MN-major SW128 tile).
+// acc[128 x D] (+)= A[128 x 128] (16-bit in TMEM, K-major) * B[128 x D] (MN-major tile).
 // A is stored in two halves, one per compute warpgroup: K columns 0-63 packed in TMEM columns
 // [a, a + 32), K columns 64-127 in [a + 64, a + 96) (each warpgroup writes into the first half of
 // its own column range, so it never overwrites values the other warpgroup has yet to read).
@@ -126,17 +163,8 @@ __device__ __forceinline__ void umma_tmem_tile(uint32_t d_tmem, uint32_t a_tmem,
   constexpr uint32_t IDESC = idesc_f16(BF16, kBT, D, false, true);
 #pragma unroll
   for (int k = 0; k < kBT / 16; ++k)
-    umma_ts(d_tmem, a_tmem + (k / 4) * 64 + (k % 4) * 8, desc_add(b_desc, k * 2048), IDESC, (acc | k) ? 1u : 0u);
-}
-
-// acc[128 x D] (+)= A[128 x 128] (K-major SW128 in shared memory) * B[128 x D] (MN-major SW128).
-template <int D, bool BF16>
-__device__ __forceinline__ void umma_smem_tile(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t acc) {
-  constexpr uint32_t IDESC = idesc_f16(BF16, kBT, D, false, true);
-#pragma unroll
-  for (int k = 0; k < kBT / 16; ++k)
-    umma_ss(d_tmem, desc_add(a_desc, (k / 4) * (kBT * 128) + (k % 4) * 32), desc_add(b_desc, k * 2048),
-            IDESC, (acc | k) ? 1u : 0u);
+    umma_ts(d_tmem, a_tmem + (k / 4) * 64 + (k % 4) * 8, desc_add(b_desc, k * BwdTile<D>::kRowStep), IDESC,
+            (acc | k) ? 1u : 0u);
 }
 
 struct BwdSmem {
@@ -270,17 +298,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const uint64_t pol_once = policy_evict_first();
         const uint64_t pol_shared = policy_evict_last();
         mbar_arrive_expect_tx(BAR(DQ_OUTER), 2 * C::kTile);
-        for (int c = 0; c < D / 64; ++c) {
-          tma_load_3d(sQ + c * (kBT * 128), &tmQ, BAR(DQ_OUTER), c * 64, i * kBT, bh, pol_once);
-          tma_load_3d(sdO + c * (kBT * 128), &tmdO, BAR(DQ_OUTER), c * 64, i * kBT, bh, pol_once);
-        }
+        load_tile<D>(sQ, &tmQ, BAR(DQ_OUTER), i * kBT, bh, pol_once);
+        load_tile<D>(sdO, &tmdO, BAR(DQ_OUTER), i * kBT, bh, pol_once);
         int issued = 0;
         for (int s = 0; s < nsteps; ++s) {
           const int st = s % KST;
           if (!mbar_wait(BAR(DQ_KEMPTY + st), ((s / KST) & 1) ^ 1, p.status, kDevTimeoutBwd)) break;
           mbar_arrive_expect_tx(BAR(DQ_KFULL + st), C::kTile);
-          for (int c = 0; c < D / 64; ++c)
-            tma_load_3d(sK + st * C::kTile + c * (kBT * 128), &tmK, BAR(DQ_KFULL + st), c * 64, s * kBT, bkv, pol_shared);
+          load_tile<D>(sK + st * C::kTile, &tmK, BAR(DQ_KFULL + st), s * kBT, bkv, pol_shared);
           ++issued;
         }
         drain_wait(BAR(DQ_OUTER), 0, p.status);
@@ -296,8 +321,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const int st = s % VST;
           if (!mbar_wait(BAR(DQ_VEMPTY + st), ((s / VST) & 1) ^ 1, p.status, kDevTimeoutBwd)) break;
           mbar_arrive_expect_tx(BAR(DQ_VFULL + st), C::kTile);
-          for (int c = 0; c < D / 64; ++c)
-            tma_load_3d(sV + st * C::kTile + c * (kBT * 128), &tmV, BAR(DQ_VFULL + st), c * 64, s * kBT, bkv, pol_shared);
+          load_tile<D>(sV + st * C::kTile, &tmV, BAR(DQ_VFULL + st), s * kBT, bkv, pol_shared);
           ++issued;
         }
         for (int s = max(0, issued - VST); s < issued; ++s) drain_wait(BAR(DQ_VFULL + s % VST), (s / VST) & 1, p.status);
@@ -306,9 +330,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     } else if (warp == kBwdWarpMma) {
       // ---------------- UMMA issuer
       if (lane == 0) {
-        const uint64_t dQd = sdesc_sw128(sQ, 16, 1024), dOd = sdesc_sw128(sdO, 16, 1024);
-        const uint64_t dKk = sdesc_sw128(sK, 16, 1024), dVk = sdesc_sw128(sV, 16, 1024);
-        const uint64_t dKm = sdesc_sw128(sK, kBT * 128, 1024);
+        const uint64_t dQd = kmajor_desc<D>(sQ), dOd = kmajor_desc<D>(sdO);
+        const uint64_t dKk = kmajor_desc<D>(sK), dVk = kmajor_desc<D>(sV);
+        const uint64_t dKm = mnmajor_desc<D>(sK);
         bool ok = mbar_wait(BAR(DQ_OUTER), 0, p.status, kDevTimeoutBwd) &&
                   mbar_wait(BAR(DQ_KFULL + 0), 0, p.status, kDevTimeoutBwd) &&
                   mbar_wait(BAR(DQ_VFULL + 0), 0, p.status, kDevTimeoutBwd);
@@ -409,11 +433,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_after();
       uint8_t* orow = reinterpret_cast<uint8_t*>(p.dq) + ridx * (D * 2);
 #pragma unroll 1
-      for (int c = w * (D / 64); c < (w + 1) * (D / 64); ++c) {
-        uint32_t v[32];
-        tmem_ld32(tDQ + lane_off + c * 32, v);
-        tmem_ld_wait(v);
-        if (qrow < p.S) store_row_chunk<BF16>(orow + c * 64, v, p.sm_scale);
+      if constexpr (D >= 64) {
+        for (int c = w * (D / 64); c < (w + 1) * (D / 64); ++c) {  // 32-column chunks
+          uint32_t v[32];
+          tmem_ld32(tDQ + lane_off + c * 32, v);
+          tmem_ld_wait(v);
+          if (qrow < p.S) store_row_chunk<BF16>(orow + c * 64, v, p.sm_scale);
+        }
+      } else {  // D = 32: each warpgroup stores 16 columns (32 bytes) of its row
+        uint32_t v[16];
+        tmem_ld16(tDQ + lane_off + w * 16, v);
+        tmem_ld_wait16(v);
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          pk[i] = pack2<BF16>(__uint_as_float(v[2 * i]) * p.sm_scale, __uint_as_float(v[2 * i + 1]) * p.sm_scale);
+        if (qrow < p.S) {
+          uint4* d = reinterpret_cast<uint4*>(orow + w * 32);
+          d[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          d[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        }
       }
     }
   }
@@ -505,10 +544,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const uint64_t pol_once = policy_evict_first();
         const uint64_t pol_shared = policy_evict_last();
         mbar_arrive_expect_tx(BAR(KV_OUTER), 2 * C::kTile);
-        for (int c = 0; c < D / 64; ++c) {
-          tma_load_3d(sK + c * (kBT * 128), &tmK, BAR(KV_OUTER), c * 64, j * kBT, bkv, pol_once);
-          tma_load_3d(sV + c * (kBT * 128), &tmV, BAR(KV_OUTER), c * 64, j * kBT, bkv, pol_once);
-        }
+        load_tile<D>(sK, &tmK, BAR(KV_OUTER), j * kBT, bkv, pol_once);
+        load_tile<D>(sV, &tmV, BAR(KV_OUTER), j * kBT, bkv, pol_once);
         int issued = 0;
         for (int s = 0; s < nsteps; ++s) {
           const int st = s % QST;
@@ -517,9 +554,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const int bh = b * p.H + g * p.group + hh;
           const int rows = min(kBT, p.S - it * kBT);  // a multiple of 64 (S % 64 == 0)
           mbar_arrive_expect_tx(BAR(KV_QFULL + st), C::kTile + rows * 4);
-          for (int c = 0; c < D / 64; ++c)
-            tma_load_3d(sQ + st * C::kTile + c * (kBT * 128), &tmQ, BAR(KV_QFULL + st), c * 64, it * kBT, bh,
-                        pol_shared);
+          load_tile<D>(sQ + st * C::kTile, &tmQ, BAR(KV_QFULL + st), it * kBT, bh, pol_shared);
           bulk_load(sm.base + C::kOffLse + st * C::kStat, p.lse + static_cast<size_t>(bh) * p.S + it * kBT,
                     rows * 4, BAR(KV_QFULL + st));
           ++issued;
@@ -540,9 +575,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const int bh = b * p.H + g * p.group + hh;
           const int rows = min(kBT, p.S - it * kBT);
           mbar_arrive_expect_tx(BAR(KV_OFULL + st), C::kTile + rows * 4);
-          for (int c = 0; c < D / 64; ++c)
-            tma_load_3d(sdO + st * C::kTile + c * (kBT * 128), &tmdO, BAR(KV_OFULL + st), c * 64, it * kBT, bh,
-                        pol_shared);
+          load_tile<D>(sdO + st * C::kTile, &tmdO, BAR(KV_OFULL + st), it * kBT, bh, pol_shared);
           bulk_load(sm.base + C::kOffDelta + st * C::kStat, p.delta + static_cast<size_t>(bh) * p.S + it * kBT,
                     rows * 4, BAR(KV_OFULL + st));
           ++issued;
@@ -557,9 +590,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // current one (S^T(s+1) follows PREADY(s), dP^T(s+1) follows DSREADY(s)), so no barrier can
       // run two phases ahead of the parity waited on.
       if (lane == 0) {
-        const uint64_t dKd = sdesc_sw128(sK, 16, 1024), dVd = sdesc_sw128(sV, 16, 1024);
-        const uint64_t dQk = sdesc_sw128(sQ, 16, 1024), dOk = sdesc_sw128(sdO, 16, 1024);
-        const uint64_t dQm = sdesc_sw128(sQ, kBT * 128, 1024), dOm = sdesc_sw128(sdO, kBT * 128, 1024);
+        const uint64_t dKd = kmajor_desc<D>(sK), dVd = kmajor_desc<D>(sV);
+        const uint64_t dQk = kmajor_desc<D>(sQ), dOk = kmajor_desc<D>(sdO);
+        const uint64_t dQm = mnmajor_desc<D>(sQ), dOm = mnmajor_desc<D>(sdO);
         bool ok = mbar_wait(BAR(KV_OUTER), 0, p.status, kDevTimeoutBwd) &&
                   mbar_wait(BAR(KV_QFULL + 0), 0, p.status, kDevTimeoutBwd) &&
                   mbar_wait(BAR(KV_OFULL + 0), 0, p.status, kDevTimeoutBwd);
@@ -733,6 +766,7 @@ cudaError_t launch_dq_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CU
 }  // namespace
 
 cudaError_t launch_bwd_preprocess(const BwdParams& p, bool bf16, cudaStream_t stream) {
+  if (p.D == 32) return bf16 ? launch_pre_t<32, true>(p, stream) : launch_pre_t<32, false>(p, stream);
   if (p.D == 64) return bf16 ? launch_pre_t<64, true>(p, stream) : launch_pre_t<64, false>(p, stream);
   if (p.D == 128) return bf16 ? launch_pre_t<128, true>(p, stream) : launch_pre_t<128, false>(p, stream);
   return cudaErrorInvalidValue;
@@ -740,6 +774,8 @@ cudaError_t launch_bwd_preprocess(const BwdParams& p, bool bf16, cudaStream_t st
 
 cudaError_t launch_bwd_dkdv(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
                             const CUtensorMap& tmdO, const BwdParams& p, bool bf16, cudaStream_t stream) {
+  if (p.D == 32) return bf16 ? launch_dkdv_t<32, true>(tmQ, tmK, tmV, tmdO, p, stream)
+                             : launch_dkdv_t<32, false>(tmQ, tmK, tmV, tmdO, p, stream);
   if (p.D == 64) return bf16 ? launch_dkdv_t<64, true>(tmQ, tmK, tmV, tmdO, p, stream)
                              : launch_dkdv_t<64, false>(tmQ, tmK, tmV, tmdO, p, stream);
   if (p.D == 128) return bf16 ? launch_dkdv_t<128, true>(tmQ, tmK, tmV, tmdO, p, stream)
@@ -749,6 +785,8 @@ cudaError_t launch_bwd_dkdv(const CUtensorMap& tmQ, const CUtensorMap& tmK, cons
 
 cudaError_t launch_bwd_dq(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
                           const CUtensorMap& tmdO, const BwdParams& p, bool bf16, cudaStream_t stream) {
+  if (p.D == 32) return bf16 ? launch_dq_t<32, true>(tmQ, tmK, tmV, tmdO, p, stream)
+                             : launch_dq_t<32, false>(tmQ, tmK, tmV, tmdO, p, stream);
   if (p.D == 64) return bf16 ? launch_dq_t<64, true>(tmQ, tmK, tmV, tmdO, p, stream)
                              : launch_dq_t<64, false>(tmQ, tmK, tmV, tmdO, p, stream);
   if (p.D == 128) return bf16 ? launch_dq_t<128, true>(tmQ, tmK, tmV, tmdO, p, stream)

@@ -58,7 +58,7 @@ extern "C" int fa_bwd_noalloc(const void* q, const void* k, const void* v, const
   if (B < 1 || H < 1 || H_kv < 1 || S < 1 || H % H_kv != 0) return FA_ERR_INVALID_ARG;
   if (static_cast<long long>(B) * H * S > FA_NOALLOC_MAX_ROWS) return FA_ERR_TOO_LARGE;
   if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_ERR_UNSUPPORTED;
-  if (D != 64 && D != 128) return FA_ERR_UNSUPPORTED;
+  if (D != 32 && D != 64 && D != 128) return FA_ERR_UNSUPPORTED;
   if ((tile_m != 64 && tile_m != 128) || (tile_n != 64 && tile_n != 128)) return FA_ERR_UNSUPPORTED;
   if (S % 64 != 0) return FA_ERR_UNSUPPORTED;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(dO) ||

@@ -17,8 +17,7 @@
  *
  * Layouts: q, o, dq, do = [B, H, S, D]; k, v, dk, dv = [B, H_kv, S, D] (H_kv divides H; query
  * head h reads K/V head h / (H / H_kv)); lse, delta = [B, H, S] float32.
- * dtype: FA_DTYPE_F16 or FA_DTYPE_BF16 (all 16-bit tensors share it); D in {32, 64, 128} for
- * fa_fwd, D in {64, 128} for the backward entry points.
+ * dtype: FA_DTYPE_F16 or FA_DTYPE_BF16 (all 16-bit tensors share it); D in {32, 64, 128}.
  * Accumulation and softmax are float32.  lse is the log2-domain log-sum-exp of the scaled
  * scores:  lse[r] = log2( sum_{c <= r} 2^(log2(e) * q_r . k_c / sqrt(D)) ).
  */

@@ -75,7 +75,7 @@ def test_reference_backward_cases(case, cuda_device):
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("H,H_kv,D", [(8, 2, 128), (4, 1, 64), (6, 3, 64), (4, 4, 128)])
+@pytest.mark.parametrize("H,H_kv,D", [(8, 2, 128), (4, 1, 64), (6, 3, 64), (4, 4, 128), (4, 4, 32), (8, 2, 32)])
 def test_gqa_backward_vs_oracle(dtype, H, H_kv, D, cuda_device):
     B, N = 2, 384
     q = seeded(f"bq{H}{H_kv}{D}", (B, H, N, D), dtype)

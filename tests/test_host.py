@@ -65,15 +65,16 @@ def test_c_abi_rejects_bad_arguments_before_touching_the_device(kw, code):
     assert _fwd_rc(**kw) == code
 
 
-def test_backward_rejects_head_dim_32_before_touching_the_device():
-    """D = 32 is a forward head dim only: every backward entry point answers FA_ERR_UNSUPPORTED."""
+def test_backward_rejects_unsupported_head_dims_before_touching_the_device():
+    """Head dims outside {32, 64, 128} answer FA_ERR_UNSUPPORTED from every backward entry point."""
     lib = _native().load()
     vp = ctypes.c_void_p
     p = vp(16)
-    assert lib.fa_bwd_preprocess(p, p, p, 1, 8, 128, 32, 0, p, None) == 2
-    assert lib.fa_bwd_dkdv(p, p, p, p, p, p, p, p, 1, 8, 8, 128, 32, 0, 64, 64, p, None) == 2
-    assert lib.fa_bwd_dq(p, p, p, p, p, p, p, 1, 8, 8, 128, 32, 0, 64, 64, p, None) == 2
-    assert lib.fa_bwd_noalloc(p, p, p, p, p, p, p, p, p, 1, 8, 8, 128, 32, 0, 64, 64, p, None) == 2
+    for D in (48, 96, 256):
+        assert lib.fa_bwd_preprocess(p, p, p, 1, 8, 128, D, 0, p, None) == 2
+        assert lib.fa_bwd_dkdv(p, p, p, p, p, p, p, p, 1, 8, 8, 128, D, 0, 64, 64, p, None) == 2
+        assert lib.fa_bwd_dq(p, p, p, p, p, p, p, 1, 8, 8, 128, D, 0, 64, 64, p, None) == 2
+        assert lib.fa_bwd_noalloc(p, p, p, p, p, p, p, p, p, 1, 8, 8, 128, D, 0, 64, 64, p, None) == 2
 
 
 def test_python_wrappers_keep_reference_errors():
