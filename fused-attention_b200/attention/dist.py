@@ -69,8 +69,10 @@ MIN_UNITS_PER_CHUNK = 8
 def max_chunks(world):
     """The copy engines sit idle while a pass computes its first chunk and the last chunk's
     copies run after the kernels: finer chunks shorten both, at the price of more, smaller
-    launches.  The gathered bytes per rank grow with world - 1, so larger worlds take more."""
-    return 8 if world >= 4 else 4
+    launches.  Four is the measured choice: at 16 heads per launch (eight chunks of the bench's
+    128 units) the forward runs at about 64 % of its full-grid rate, which costs more than the
+    shorter exposed copies save."""
+    return 4
 
 
 def plan_chunks(units, world):

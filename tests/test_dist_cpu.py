@@ -133,7 +133,7 @@ def test_chunk_layout():
     import sys
     sys.path.insert(0, os.path.join(REPO, "fused-attention_b200"))
     from attention.dist import chunk_ranges, plan_chunks
-    assert plan_chunks(128 * 8, 8) == 8 and plan_chunks(128 * 2, 2) == 4
+    assert plan_chunks(128 * 8, 8) == 4 and plan_chunks(128 * 2, 2) == 4
     assert plan_chunks(16, 2) == 1 and plan_chunks(32, 2) == 2
     with pytest.raises(ValueError):
         plan_chunks(10, 4)
