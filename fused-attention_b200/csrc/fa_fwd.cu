@@ -10,18 +10,23 @@
 // CTA work unit: two 128-row query tiles that read the SAME K/V head:
 //   mode 0: q-tiles (2c, 2c+1) of one head          (MHA, odd GQA groups)
 //   mode 1: q-tile i of query heads (2p, 2p+1)      (even GQA groups: K/V tile shared)
-// Warp roles (384 threads, warpgroup aligned):
-//   warps 0-3   softmax for tile 0 (one TMEM lane = one query row per thread)
-//   warps 4-7   softmax for tile 1
-//   warp 8      TMA producer: Q tiles once, then the K ring (K(j) is freed once every tile's
+// Grid order: bands of up to 16 work units, every unit's heaviest tile pair first inside a band
+// (see band_order), so the grid ends with its shortest CTAs.
+// Warp roles (640 threads):
+//   warps 0-15  four softmax warpgroups: warpgroup g serves query tile t = g / 2 and key-column
+//               half h = g % 2 (one TMEM lane = one query row per thread, BN/2 columns); the two
+//               halves of a row exchange partial maxima (and, at the end, partial sums) through
+//               shared memory behind one named barrier per tile
+//   warp 16     TMA producer: Q tiles once, then the K ring (K(j) is freed once every tile's
 //               Q K^T has read it, well before V(j) is freed, so K loads run ahead)
-//   warp 9      UMMA issuer (one thread): S_t = Q_t K_j^T into TMEM, O_t += P_t V_j with P_t
+//   warp 17     UMMA issuer (one thread): S_t = Q_t K_j^T into TMEM, O_t += P_t V_j with P_t
 //               read from TMEM; descriptors are precomputed and advanced by constant offsets
-//   warp 10     TMA producer: the V ring
-//   warp 11     idle
+//   warp 18     TMA producer: the V ring
+//   warp 19     idle
 // TMEM (512 columns): S_0 | S_1 | O_0 | O_1, 128 columns each; P_t (16-bit) overwrites the first
-// half of S_t once the row has been read into registers.  The two softmax warpgroups ping-pong:
-// while one converts its S tile the tensor core runs the other tile's P V and next Q K^T.
+// half of each warpgroup's own S_t columns once the row has been read into registers.  The two
+// tiles ping-pong: while one tile's warpgroups turn S into P, the tensor core runs the other
+// tile's P V and next Q K^T.
 // O is rescaled in TMEM only when a row max grows by more than 2^8 (otherwise the stale max is
 // kept, which is exact because numerator and denominator use the same offset).
 #include "fa_internal.h"
