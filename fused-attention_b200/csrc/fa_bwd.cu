@@ -745,7 +745,8 @@ template <int D, bool BF16>
 cudaError_t launch_dkdv_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
                           const CUtensorMap& tmdO, const BwdParams& p, cudaStream_t stream) {
   auto kern = bwd_dkdv_kernel<D, BF16>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemOptin);
+  static std::atomic<bool> smem_set[64];
+  cudaError_t e = opt_in_smem(kern, kSmemOptin, smem_set);
   if (e != cudaSuccess) return e;
   const int nkt = (p.S + kBT - 1) / kBT;
   kern<<<p.B * p.H_kv * nkt, kBwdThreads, kSmemOptin, stream>>>(tmQ, tmK, tmV, tmdO, p);
@@ -756,7 +757,8 @@ template <int D, bool BF16>
 cudaError_t launch_dq_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
                         const CUtensorMap& tmdO, const BwdParams& p, cudaStream_t stream) {
   auto kern = bwd_dq_kernel<D, BF16>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemOptin);
+  static std::atomic<bool> smem_set[64];
+  cudaError_t e = opt_in_smem(kern, kSmemOptin, smem_set);
   if (e != cudaSuccess) return e;
   const int nqt = (p.S + kBT - 1) / kBT;
   kern<<<p.B * p.H * nqt, kBwdThreads, kSmemOptin, stream>>>(tmQ, tmK, tmV, tmdO, p);

@@ -544,7 +544,8 @@ cudaError_t launch_fwd_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const C
                          const FwdParams& p, cudaStream_t stream) {
   using C = FwdCfg<D, BN>;
   auto kern = fa_fwd_kernel<D, BN, BF16>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  static std::atomic<bool> smem_set[64];
+  cudaError_t e = opt_in_smem(kern, C::kSmemBytes, smem_set);
   if (e != cudaSuccess) return e;
   kern<<<p.n_items, kThreads, C::kSmemBytes, stream>>>(tmQ, tmK, tmV, p);
   return cudaGetLastError();

@@ -3,6 +3,7 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <atomic>
 #include <cstdint>
 
 namespace fa {
@@ -48,6 +49,20 @@ struct BwdParams {
 // Work units (heads, head pairs) whose tiles are launched heavy-first together: up to 16 units,
 // about 64 MiB of K/V at S = 8192, D = 128, so the heads in flight keep their K/V in the 126 MB L2.
 inline int work_band(long long units) { return units < 16 ? static_cast<int>(units) : 16; }
+
+// Opt a kernel into `bytes` of dynamic shared memory once per device (the attribute is a
+// per-function, per-device setting; setting it on every launch costs host time on short calls).
+// `done` is the kernel's own flag array; devices past its size set the attribute every time.
+template <typename Kernel>
+inline cudaError_t opt_in_smem(Kernel kernel, int bytes, std::atomic<bool> (&done)[64]) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < 64 && done[dev].load(std::memory_order_acquire)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev].store(true, std::memory_order_release);
+  return e;
+}
 
 // Launchers implemented in the kernel translation units.  They return a cudaError_t.
 cudaError_t launch_fwd(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
