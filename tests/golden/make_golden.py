@@ -61,8 +61,11 @@ def lse_from_reference_scores(q, k, group):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("FA_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("FA_REFERENCE_ROOT"),
+                    help="root of a checkout of the reference project (or set FA_REFERENCE_ROOT)")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("pass --reference PATH (a checkout of the reference project) or set FA_REFERENCE_ROOT")
     ref = a.reference
     sys.path.insert(0, ref)
     cases = _load(os.path.join(ref, "tests/fused/cases.py"), "ref_cases")
