@@ -333,14 +333,17 @@ def main():
     # and slice c-1 copies out on another (PCIe is full duplex).  Every byte of Q, K, V, dO goes
     # in and every byte of O, dQ, dK, dV comes out inside the timed region.  A slice is `world`
     # batch entries, so with N GPUs each rank still gets a full share of every call; on one GPU
-    # with MHA each batch entry is cut into two head halves (contiguous, independent), which
-    # halves the copy-in of the first slice and the copy-out of the last, the parts no compute
-    # can hide.
+    # with MHA each batch entry is cut into head groups (contiguous, independent) so that a step
+    # has about 16 slices: that shortens the copy-in of the first slice and the copy-out of the
+    # last, the parts no compute can hide (the PCIe copies, not the kernels, bound this leg).
     h2d_stream = torch.cuda.Stream(device=dev)
     d2h_stream = torch.cuda.Stream(device=dev)
     comp = torch.cuda.current_stream(dev)
     bs = world
-    hsplit = 2 if (world == 1 and H_kv == H and H % 2 == 0) else 1
+    hsplit = 1
+    if world == 1 and H_kv == H:
+        while hsplit * 2 * (B // bs) <= 16 and H % (hsplit * 2) == 0:
+            hsplit *= 2
     hh = H // hsplit
     slices = [(slice(c * bs, (c + 1) * bs), slice(p * hh, (p + 1) * hh))
               for c in range(B // bs) for p in range(hsplit)]
