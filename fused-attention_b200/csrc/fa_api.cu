@@ -76,6 +76,8 @@ int check_device() {
   return ok == 1 ? FA_OK : FA_ERR_DEVICE;
 }
 
+// Argument checks that need no device: every entry point runs them (and its alignment checks)
+// before check_device(), so a bad argument is reported the same way with or without a GPU.
 int check_common(int B, int H, int H_kv, int S, int D, int dtype, int tile_m, int tile_n,
                  const int* dev_status) {
   if (B < 1 || H < 1 || H_kv < 1 || S < 1) return FA_ERR_INVALID_ARG;
@@ -86,7 +88,7 @@ int check_common(int B, int H, int H_kv, int S, int D, int dtype, int tile_m, in
   if ((tile_m != 64 && tile_m != 128) || (tile_n != 64 && tile_n != 128)) return FA_ERR_UNSUPPORTED;
   // Every index the kernels form fits in 32 bits per head, 64 bits overall.
   if (static_cast<long long>(B) * H > (1LL << 30) || S > (1 << 24)) return FA_ERR_UNSUPPORTED;
-  return check_device();
+  return FA_OK;
 }
 
 }  // namespace
@@ -120,6 +122,7 @@ int fa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) ||
       (lse && (reinterpret_cast<uintptr_t>(lse) & 3u)))
     return FA_ERR_ALIGNMENT;
+  if ((rc = check_device()) != FA_OK) return rc;
 
   CUtensorMap tmQ, tmK, tmV;
   if ((rc = make_map(&tmQ, q, B * H, S, D, dtype, 128)) != FA_OK) return rc;
@@ -155,6 +158,7 @@ int fa_bwd_preprocess(const void* o, const void* dO, float* delta, int B, int H,
   if (rc != FA_OK) return rc;
   if (!aligned16(o) || !aligned16(dO) || (reinterpret_cast<uintptr_t>(delta) & 3u))
     return FA_ERR_ALIGNMENT;
+  if ((rc = check_device()) != FA_OK) return rc;
   fa::BwdParams p{};
   p.o = o;
   p.dO = dO;
@@ -183,6 +187,7 @@ static int bwd_prepare(const void* q, const void* k, const void* v, const void* 
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(dO) || !aligned16(lse) ||
       !aligned16(delta))
     return FA_ERR_ALIGNMENT;
+  if ((rc = check_device()) != FA_OK) return rc;
   if ((rc = make_map(tmQ, q, B * H, S, D, dtype, q_rows)) != FA_OK) return rc;
   if ((rc = make_map(tmK, k, B * H_kv, S, D, dtype, kv_rows)) != FA_OK) return rc;
   if ((rc = make_map(tmV, v, B * H_kv, S, D, dtype, kv_rows)) != FA_OK) return rc;

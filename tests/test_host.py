@@ -65,6 +65,23 @@ def test_c_abi_rejects_bad_arguments_before_touching_the_device(kw, code):
     assert _fwd_rc(**kw) == code
 
 
+def test_alignment_and_shape_rules_are_checked_before_the_device():
+    """Misaligned bases answer FA_ERR_ALIGNMENT and a backward S that is not a multiple of 64
+    FA_ERR_UNSUPPORTED, with or without a GPU; a well-formed call on a machine without an sm_100
+    device answers a CUDA / device error, never FA_OK."""
+    lib = _native().load()
+    vp = ctypes.c_void_p
+    a, m = vp(256), vp(264)  # 16-byte aligned, misaligned
+    assert _fwd_rc(q=264, k=256, v=256, o=256) == 3
+    assert _fwd_rc(q=256, k=256, v=256, o=256, lse=ctypes.c_void_p(258)) == 3
+    assert lib.fa_bwd_preprocess(m, a, a, 1, 8, 128, 64, 0, a, None) == 3
+    assert lib.fa_bwd_dkdv(a, a, a, a, a, a, m, a, 1, 8, 8, 128, 64, 0, 64, 64, a, None) == 3
+    assert lib.fa_bwd_dq(a, a, a, a, a, a, a, 1, 8, 8, 96, 64, 0, 64, 64, a, None) == 2  # S % 64
+    assert lib.fa_bwd_noalloc(a, a, a, a, a, a, a, a, m, 1, 8, 8, 128, 64, 0, 64, 64, a, None) == 3
+    if not torch.cuda.is_available():
+        assert _fwd_rc(q=256, k=256, v=256, o=256) in (4, 5, 6)  # CUDA, driver or device error
+
+
 def test_backward_rejects_unsupported_head_dims_before_touching_the_device():
     """Head dims outside {32, 64, 128} answer FA_ERR_UNSUPPORTED from every backward entry point."""
     lib = _native().load()
@@ -144,3 +161,19 @@ def test_cli_exit_codes(tmp_path):
     rc, err = _cli("run_attention_gqa.py", "--input", str(good), "--output", str(tmp_path / "o.npy"),
                    "--backend", "unfused")
     assert rc == 1 and "not built" in err
+
+
+def test_bench_reference_arm_prints_the_contract_line():
+    """`bench.py --impl reference` (CPU only) prints one JSON line with the keys the driver reads."""
+    import json
+    r = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference", "--steps", "1",
+                        "--warmup", "0", "--seq", "256", "--dim", "64"], capture_output=True, text=True,
+                       timeout=600, env={**os.environ, "CUDA_VISIBLE_DEVICES": ""})
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    for key in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "config", "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["impl"] == "reference" and line["value"] > 0
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
