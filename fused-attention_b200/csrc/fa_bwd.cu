@@ -76,19 +76,16 @@ constexpr int kBT = 128;  // tile rows (outer and inner)
 constexpr uint32_t kBwdTmemCols = 512;
 constexpr int kSmemOptin = 232448;  // max dynamic shared memory per block on sm_100
 
-// P = 2^(s * scale - m) for 64 values (m given per pair), fp32 results; 6 of every 16 pairs on
-// the FMA-pipe polynomial, the rest on MUFU ex2.
+// P = 2^(s * scale - m) for kN values (m given per pair), fp32 results, every exp2 on MUFU ex2
+// (an FMA-pipe polynomial for part of them measured 3-8 % slower: these phases are bound by
+// their instruction stream, not by MUFU throughput).
 template <int kN>
 __device__ __forceinline__ void exp2_row(const uint32_t* s, const float* neg_m, float scale, float* out) {
   const uint64_t scale2 = f2(scale, scale);
 #pragma unroll
   for (int i = 0; i < kN / 2; ++i) {
     const uint64_t x2 = ffma2(f2u(s[2 * i], s[2 * i + 1]), scale2, f2(neg_m[2 * i], neg_m[2 * i + 1]));
-    uint64_t p2;
-    if ((0x5252u >> (i & 15)) & 1u)
-      p2 = exp2_poly2(f2lo(x2), f2hi(x2));
-    else
-      p2 = f2(ex2_approx(f2lo(x2)), ex2_approx(f2hi(x2)));
+    const uint64_t p2 = f2(ex2_approx(f2lo(x2)), ex2_approx(f2hi(x2)));
     out[2 * i] = f2lo(p2);
     out[2 * i + 1] = f2hi(p2);
   }

@@ -134,22 +134,17 @@ __device__ __forceinline__ Work decode_work(const FwdParams& p, int item) {
   return w;
 }
 
-// P = 2^(S * scale - m) for 32 columns of one row: packed f32x2 math; on unmasked tiles the pairs
-// in kPolyPairs (6 of 16) use the FMA-pipe polynomial, the rest the MUFU ex2, which balances the
-// two pipes.  Masked tiles use MUFU only, so masked entries (-inf) give exactly 0.
-constexpr uint32_t kPolyPairs = 0x5252u;  // pairs 1, 4, 6, 9, 12, 14
-
-template <bool kPoly, bool BF16>
+// P = 2^(S * scale - m) for 32 columns of one row: packed f32x2 math around MUFU ex2 (masked
+// entries, -inf, give exactly 0).  Every exp2 goes to the MUFU pipe: evaluating part of them as a
+// polynomial on the FMA pipe costs more instructions than it saves MUFU time, and the softmax is
+// bound by its instruction stream, not by MUFU throughput (measured 5-6 % slower forward).
+template <bool BF16>
 __device__ __forceinline__ void softmax_chunk(const uint32_t (&r)[32], uint64_t scale2, uint64_t negm2,
                                               uint64_t (&sum2)[4], uint32_t (&pk)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const uint64_t x2 = ffma2(f2u(r[2 * i], r[2 * i + 1]), scale2, negm2);
-    uint64_t p2;
-    if (kPoly && ((kPolyPairs >> i) & 1u))
-      p2 = exp2_poly2(f2lo(x2), f2hi(x2));
-    else
-      p2 = f2(ex2_approx(f2lo(x2)), ex2_approx(f2hi(x2)));
+    const uint64_t p2 = f2(ex2_approx(f2lo(x2)), ex2_approx(f2hi(x2)));
     sum2[i & 3] = fadd2(sum2[i & 3], p2);
     pk[i] = pack2<BF16>(f2lo(p2), f2hi(p2));
   }
@@ -406,15 +401,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (key > qrow || key >= p.S) r[c][i] = __float_as_uint(-INFINITY);
               }
           }
-          float mx8[8];
+          // three-input max (sm_100): half the instructions of a two-input chain
+          float mx4[4];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) mx8[u] = -INFINITY;
+          for (int u = 0; u < 4; ++u) mx4[u] = -INFINITY;
 #pragma unroll
           for (int c = 0; c < HC / 32; ++c)
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mx8[i % 8] = fmaxf(mx8[i % 8], __uint_as_float(r[c][i]));
-          mx_half = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                          fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            for (int i = 0; i < 32; i += 2)
+              mx4[(i / 2) % 4] = fmax3(mx4[(i / 2) % 4], __uint_as_float(r[c][i]), __uint_as_float(r[c][i + 1]));
+          mx_half = fmaxf(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3]);
           // full row max: exchange with the other half (double-buffered by KV-step parity)
           xm[h * kBM + row] = mx_half;
         }
@@ -445,10 +441,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           uint32_t pk[16];
+          // Two call sites on purpose: diagonal and interior tiles get separately scheduled
+          // copies.  With one shared call site ptxas goes over the 96-register cap of this
+          // 640-thread block and spills (-Xptxas -v: 12-16 bytes for BN = 128).
           if (masked)
-            softmax_chunk<false, BF16>(rc, scale2, negm2, sum2, pk);
+            softmax_chunk<BF16>(rc, scale2, negm2, sum2, pk);
           else
-            softmax_chunk<true, BF16>(rc, scale2, negm2, sum2, pk);
+            softmax_chunk<BF16>(rc, scale2, negm2, sum2, pk);
           tmem_st16(tS + c * 16, pk);
         }
         const uint64_t s01 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));

@@ -407,34 +407,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// 2^x for a pair on the FMA pipe (relieves the MUFU pipe, which runs ex2 at 16 per clock per
-// SM).  x = n + f with n = rint(x) (via the 1.5 * 2^23 rounding constant) and f in [-1/2, 1/2];
-// 2^f ~ c0 + c1 f + c2 f^2 + c3 f^3, a minimax fit of the relative error over [-1/2, 1/2]
-// (Remez exchange; fused-attention_b200/csrc/fit_exp2_poly.py regenerates the coefficients):
-// max relative error 7.5e-5, below half an ulp of bfloat16 and ~0.3 ulp of float16.  2^n is
-// applied by adding n to the exponent field: the low 9 bits of the rounding sum hold n in two's
-// complement, so (bits(t) << 23) == n << 23.  x is clamped to >= -126 so the exponent stays >= 0;
-// results below ~2^-126 are tiny denormals instead of 0 (irrelevant for a softmax numerator).
-__device__ __forceinline__ uint64_t exp2_poly2(float x0, float x1) {
-  const uint64_t kRound = f2(12582912.0f, 12582912.0f);
-  const uint64_t kNegRound = f2(-12582912.0f, -12582912.0f);
-  const uint64_t kNegOne = f2(-1.0f, -1.0f);
-  const uint64_t c0 = f2(9.999280572e-01f, 9.999280572e-01f);
-  const uint64_t c1 = f2(6.932609677e-01f, 6.932609677e-01f);
-  const uint64_t c2 = f2(2.426111251e-01f, 2.426111251e-01f);
-  const uint64_t c3 = f2(5.517166853e-02f, 5.517166853e-02f);
-  const uint64_t x = f2(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
-  const uint64_t t = fadd2(x, kRound);       // rint(x) in the low mantissa bits
-  const uint64_t n = fadd2(t, kNegRound);    // rint(x) as a float
-  const uint64_t fr = ffma2(n, kNegOne, x);  // x - rint(x)
-  uint64_t p = ffma2(c3, fr, c2);
-  p = ffma2(p, fr, c1);
-  p = ffma2(p, fr, c0);
-  const uint32_t lo = static_cast<uint32_t>(p) + (static_cast<uint32_t>(t) << 23);
-  const uint32_t hi = static_cast<uint32_t>(p >> 32) + (static_cast<uint32_t>(t >> 32) << 23);
-  return f2u(lo, hi);
-}
-
 // Pack two fp32 values into one 32-bit word of 16-bit floats (lo = first / lower k index).
 template <bool kBf16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
