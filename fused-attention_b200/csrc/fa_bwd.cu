@@ -66,8 +66,8 @@ cudaError_t launch_pre_t(const BwdParams& p, cudaStream_t stream) {
 //          Q(s) is held until dK(s), so with two stages the next tile's load was exposed.
 // Warp roles (384 threads): warps 0-3 and 4-7 are two compute warpgroups splitting every tile's
 // 128 columns (each thread: one TMEM lane = one row, 64 columns); warps 8 and 10 issue TMA
-// loads; warp 9 is the single-thread UMMA issuer.  All warps run with the launch allocation of
-// 168 registers per thread.
+// loads; warp 9 issues the UMMAs (the whole warp runs the issue loop and one elected lane issues
+// each tcgen05 instruction).  All warps run with the launch allocation of 168 registers per thread.
 constexpr int kBwdThreads = 384;
 constexpr int kBwdWarpLoadA = 8;
 constexpr int kBwdWarpMma = 9;
@@ -139,7 +139,7 @@ __device__ __forceinline__ void load_tile(uint32_t dst, const CUtensorMap* map, 
     tma_load_3d(dst + c * T::kChunkBytes, map, bar, c * T::kChunkCols, row0, bh, policy);
 }
 
-// D[128 x 128] (+)= A[128 x D] * B[128 x D]^T, both K-major tiles of 128 rows.
+// D[128 x 128] (+)= A[128 x D] * B[128 x D]^T, both K-major tiles of 128 rows (issued by a whole warp).
 template <int D, bool BF16>
 __device__ __forceinline__ void umma_rows_rows(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc) {
   using T = BwdTile<D>;
@@ -147,11 +147,12 @@ __device__ __forceinline__ void umma_rows_rows(uint32_t d_tmem, uint64_t a_desc,
 #pragma unroll
   for (int k = 0; k < D / 16; ++k) {
     const uint32_t off = (k / T::kKSteps) * T::kChunkBytes + (k % T::kKSteps) * 32;
-    umma_ss(d_tmem, desc_add(a_desc, off), desc_add(b_desc, off), IDESC, k > 0 ? 1u : 0u);
+    umma_ss_w(d_tmem, desc_add(a_desc, off), desc_add(b_desc, off), IDESC, k > 0 ? 1u : 0u);
   }
 }
 
-// acc[128 x D] (+)= A[128 x 128] (16-bit in TMEM, K-major) * B[128 x D] (MN-major tile).
+// acc[128 x D] (+)= A[128 x 128] (16-bit in TMEM, K-major) * B[128 x D] (MN-major tile), issued by
+// a whole warp.
 // A is stored in two halves, one per compute warpgroup: K columns 0-63 packed in TMEM columns
 // [a, a + 32), K columns 64-127 in [a + 64, a + 96) (each warpgroup writes into the first half of
 // its own column range, so it never overwrites values the other warpgroup has yet to read).
@@ -160,7 +161,7 @@ __device__ __forceinline__ void umma_tmem_tile(uint32_t d_tmem, uint32_t a_tmem,
   constexpr uint32_t IDESC = idesc_f16(BF16, kBT, D, false, true);
 #pragma unroll
   for (int k = 0; k < kBT / 16; ++k)
-    umma_ts(d_tmem, a_tmem + (k / 4) * 64 + (k % 4) * 8, desc_add(b_desc, k * BwdTile<D>::kRowStep), IDESC,
+    umma_ts_w(d_tmem, a_tmem + (k / 4) * 64 + (k % 4) * 8, desc_add(b_desc, k * BwdTile<D>::kRowStep), IDESC,
             (acc | k) ? 1u : 0u);
 }
 
@@ -326,45 +327,45 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       __syncwarp();
     } else if (warp == kBwdWarpMma) {
       // ---------------- UMMA issuer
-      if (lane == 0) {
+      {  // the whole warp runs the issue loop; one elected lane issues each tcgen05 op
         const uint64_t dQd = kmajor_desc<D>(sQ), dOd = kmajor_desc<D>(sdO);
         const uint64_t dKk = kmajor_desc<D>(sK), dVk = kmajor_desc<D>(sV);
         const uint64_t dKm = mnmajor_desc<D>(sK);
-        bool ok = mbar_wait(BAR(DQ_OUTER), 0, p.status, kDevTimeoutBwd) &&
-                  mbar_wait(BAR(DQ_KFULL + 0), 0, p.status, kDevTimeoutBwd) &&
-                  mbar_wait(BAR(DQ_VFULL + 0), 0, p.status, kDevTimeoutBwd);
+        bool ok = warp_all(mbar_wait(BAR(DQ_OUTER), 0, p.status, kDevTimeoutBwd)) &&
+                  warp_all(mbar_wait(BAR(DQ_KFULL + 0), 0, p.status, kDevTimeoutBwd)) &&
+                  warp_all(mbar_wait(BAR(DQ_VFULL + 0), 0, p.status, kDevTimeoutBwd));
         if (ok) {
           tc_fence_after();
           umma_rows_rows<D, BF16>(tS, dQd, dKk);  // S(0) = Q K_0^T
-          umma_commit(BAR(DQ_SFULL));
+          umma_commit_w(BAR(DQ_SFULL));
           umma_rows_rows<D, BF16>(tDP, dOd, dVk);  // dP(0) = dO V_0^T
-          umma_commit(BAR(DQ_DPFULL + 0));
-          umma_commit(BAR(DQ_VEMPTY + 0));
+          umma_commit_w(BAR(DQ_DPFULL + 0));
+          umma_commit_w(BAR(DQ_VEMPTY + 0));
         }
         for (int s = 0; ok && s < nsteps; ++s) {
           if (s + 1 < nsteps) {
             const int k1 = (s + 1) % KST, v1 = (s + 1) % VST;
-            if (!(ok = mbar_wait(BAR(DQ_SFREE), s & 1, p.status, kDevTimeoutBwd))) break;
-            if (!(ok = mbar_wait(BAR(DQ_KFULL + k1), ((s + 1) / KST) & 1, p.status, kDevTimeoutBwd))) break;
+            if (!(ok = warp_all(mbar_wait(BAR(DQ_SFREE), s & 1, p.status, kDevTimeoutBwd)))) break;
+            if (!(ok = warp_all(mbar_wait(BAR(DQ_KFULL + k1), ((s + 1) / KST) & 1, p.status, kDevTimeoutBwd)))) break;
             tc_fence_after();
             umma_rows_rows<D, BF16>(tS, dQd, desc_add(dKk, k1 * C::kTile));
-            umma_commit(BAR(DQ_SFULL));
-            if (!(ok = mbar_wait(BAR(DQ_VFULL + v1), ((s + 1) / VST) & 1, p.status, kDevTimeoutBwd))) break;
+            umma_commit_w(BAR(DQ_SFULL));
+            if (!(ok = warp_all(mbar_wait(BAR(DQ_VFULL + v1), ((s + 1) / VST) & 1, p.status, kDevTimeoutBwd)))) break;
             tc_fence_after();
             umma_rows_rows<D, BF16>(tDP + 128 * ((s + 1) & 1), dOd, desc_add(dVk, v1 * C::kTile));
-            umma_commit(BAR(DQ_DPFULL + ((s + 1) & 1)));
-            umma_commit(BAR(DQ_VEMPTY + v1));
+            umma_commit_w(BAR(DQ_DPFULL + ((s + 1) & 1)));
+            umma_commit_w(BAR(DQ_VEMPTY + v1));
           }
           // dS(s) is ready.  One barrier per step parity: S(s+1) and dP(s+1) are already issued,
-          // so the compute warps can finish step s+1 before this thread looks, and a single
+          // so the compute warps can finish step s+1 before the issuer looks, and a single
           // barrier would then be two phases ahead of the parity waited on.
-          if (!(ok = mbar_wait(BAR(DQ_DSREADY + (s & 1)), (s >> 1) & 1, p.status, kDevTimeoutBwd))) break;
+          if (!(ok = warp_all(mbar_wait(BAR(DQ_DSREADY + (s & 1)), (s >> 1) & 1, p.status, kDevTimeoutBwd)))) break;
           tc_fence_after();
           umma_tmem_tile<D, BF16>(tDQ, tDP + 128 * (s & 1), desc_add(dKm, (s % KST) * C::kTile), s > 0 ? 1u : 0u);
-          umma_commit(BAR(DQ_KEMPTY + s % KST));
+          umma_commit_w(BAR(DQ_KEMPTY + s % KST));
         }
-        if (ok) umma_commit(BAR(DQ_ACC));
-        umma_commit(BAR(DQ_DRAIN));
+        if (ok) umma_commit_w(BAR(DQ_ACC));
+        umma_commit_w(BAR(DQ_DRAIN));
         drain_wait(BAR(DQ_DRAIN), 0, p.status);
       }
       __syncwarp();
@@ -586,47 +587,47 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // dP^T(s)), then dP^T(s+1).  Each barrier's next phase needs its waiter to have passed the
       // current one (S^T(s+1) follows PREADY(s), dP^T(s+1) follows DSREADY(s)), so no barrier can
       // run two phases ahead of the parity waited on.
-      if (lane == 0) {
+      {  // the whole warp runs the issue loop; one elected lane issues each tcgen05 op
         const uint64_t dKd = kmajor_desc<D>(sK), dVd = kmajor_desc<D>(sV);
         const uint64_t dQk = kmajor_desc<D>(sQ), dOk = kmajor_desc<D>(sdO);
         const uint64_t dQm = mnmajor_desc<D>(sQ), dOm = mnmajor_desc<D>(sdO);
-        bool ok = mbar_wait(BAR(KV_OUTER), 0, p.status, kDevTimeoutBwd) &&
-                  mbar_wait(BAR(KV_QFULL + 0), 0, p.status, kDevTimeoutBwd) &&
-                  mbar_wait(BAR(KV_OFULL + 0), 0, p.status, kDevTimeoutBwd);
+        bool ok = warp_all(mbar_wait(BAR(KV_OUTER), 0, p.status, kDevTimeoutBwd)) &&
+                  warp_all(mbar_wait(BAR(KV_QFULL + 0), 0, p.status, kDevTimeoutBwd)) &&
+                  warp_all(mbar_wait(BAR(KV_OFULL + 0), 0, p.status, kDevTimeoutBwd));
         if (ok) {
           tc_fence_after();
           umma_rows_rows<D, BF16>(tST, dKd, dQk);  // S^T(0) = K Q_0^T
-          umma_commit(BAR(KV_STFULL));
+          umma_commit_w(BAR(KV_STFULL));
           umma_rows_rows<D, BF16>(tDPT, dVd, dOk);  // dP^T(0) = V dO_0^T
-          umma_commit(BAR(KV_DPFULL));
+          umma_commit_w(BAR(KV_DPFULL));
         }
         for (int s = 0; ok && s < nsteps; ++s) {
           const int qs = s % QST, os = s % OST;
-          if (!(ok = mbar_wait(BAR(KV_PREADY), s & 1, p.status, kDevTimeoutBwd))) break;
+          if (!(ok = warp_all(mbar_wait(BAR(KV_PREADY), s & 1, p.status, kDevTimeoutBwd)))) break;
           tc_fence_after();
           umma_tmem_tile<D, BF16>(tDV, tST, desc_add(dOm, os * C::kTile), s > 0 ? 1u : 0u);  // dV += P^T dO
-          umma_commit(BAR(KV_OEMPTY + os));  // dO(s): read by dP^T(s) and dV(s)
+          umma_commit_w(BAR(KV_OEMPTY + os));  // dO(s): read by dP^T(s) and dV(s)
           if (s + 1 < nsteps) {
             const int q1 = (s + 1) % QST;
-            if (!(ok = mbar_wait(BAR(KV_QFULL + q1), ((s + 1) / QST) & 1, p.status, kDevTimeoutBwd))) break;
+            if (!(ok = warp_all(mbar_wait(BAR(KV_QFULL + q1), ((s + 1) / QST) & 1, p.status, kDevTimeoutBwd)))) break;
             tc_fence_after();
             umma_rows_rows<D, BF16>(tST, dKd, desc_add(dQk, q1 * C::kTile));  // S^T(s+1)
-            umma_commit(BAR(KV_STFULL));
+            umma_commit_w(BAR(KV_STFULL));
           }
-          if (!(ok = mbar_wait(BAR(KV_DSREADY), s & 1, p.status, kDevTimeoutBwd))) break;
+          if (!(ok = warp_all(mbar_wait(BAR(KV_DSREADY), s & 1, p.status, kDevTimeoutBwd)))) break;
           tc_fence_after();
           umma_tmem_tile<D, BF16>(tDK, tDPT, desc_add(dQm, qs * C::kTile), s > 0 ? 1u : 0u);  // dK += dS^T Q
-          umma_commit(BAR(KV_QEMPTY + qs));  // Q(s): read by S^T(s) and dK(s)
+          umma_commit_w(BAR(KV_QEMPTY + qs));  // Q(s): read by S^T(s) and dK(s)
           if (s + 1 < nsteps) {
             const int o1 = (s + 1) % OST;
-            if (!(ok = mbar_wait(BAR(KV_OFULL + o1), ((s + 1) / OST) & 1, p.status, kDevTimeoutBwd))) break;
+            if (!(ok = warp_all(mbar_wait(BAR(KV_OFULL + o1), ((s + 1) / OST) & 1, p.status, kDevTimeoutBwd)))) break;
             tc_fence_after();
             umma_rows_rows<D, BF16>(tDPT, dVd, desc_add(dOk, o1 * C::kTile));  // dP^T(s+1)
-            umma_commit(BAR(KV_DPFULL));
+            umma_commit_w(BAR(KV_DPFULL));
           }
         }
-        if (ok) umma_commit(BAR(KV_ACC));
-        umma_commit(BAR(KV_DRAIN));
+        if (ok) umma_commit_w(BAR(KV_ACC));
+        umma_commit_w(BAR(KV_DRAIN));
         drain_wait(BAR(KV_DRAIN), 0, p.status);
       }
       __syncwarp();

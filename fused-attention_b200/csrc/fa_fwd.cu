@@ -19,8 +19,8 @@
 //               shared memory behind one named barrier per tile
 //   warp 16     TMA producer: Q tiles once, then the K ring (K(j) is freed once every tile's
 //               Q K^T has read it, well before V(j) is freed, so K loads run ahead)
-//   warp 17     UMMA issuer (one thread): S_t = Q_t K_j^T into TMEM, O_t += P_t V_j with P_t
-//               read from TMEM; descriptors are precomputed and advanced by constant offsets
+//   warp 17     UMMA issuer (the whole warp computes descriptors, one elected lane issues):
+//               S_t = Q_t K_j^T into TMEM, O_t += P_t V_j with P_t read from TMEM
 //   warp 18     TMA producer: the V ring
 //   warp 19     idle
 // TMEM (512 columns): S_0 | S_1 | O_0 | O_1, 128 columns each; P_t (16-bit) overwrites the first
@@ -150,7 +150,8 @@ __device__ __forceinline__ void softmax_chunk(const uint32_t (&r)[32], uint64_t 
   }
 }
 
-// S = Q K^T for one 128-row query tile: D/16 UMMAs, descriptors advanced by constant offsets.
+// S = Q K^T for one 128-row query tile: D/16 UMMAs, descriptors advanced by constant offsets
+// (called by the whole issuer warp).
 template <int D, int BN, bool BF16>
 __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint64_t q_desc, uint64_t k_desc) {
   using C = FwdCfg<D, BN>;
@@ -158,7 +159,7 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint64_t q_desc, uint6
   constexpr int KS = C::kKStepsPerChunk;
 #pragma unroll
   for (int k = 0; k < D / 16; ++k) {
-    umma_ss(d_tmem, desc_add(q_desc, (k / KS) * C::kQChunkBytes + (k % KS) * 32),
+    umma_ss_w(d_tmem, desc_add(q_desc, (k / KS) * C::kQChunkBytes + (k % KS) * 32),
             desc_add(k_desc, (k / KS) * C::kKVChunkBytes + (k % KS) * 32), IDESC, k > 0 ? 1u : 0u);
   }
 }
@@ -175,7 +176,7 @@ __device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint6
   constexpr int kKeyStep = 16 * FwdCfg<D, BN>::kSwBytes;  // 16 key rows of V
 #pragma unroll
   for (int k = 0; k < BN / 16; ++k)
-    umma_ts(o_tmem, p_tmem + (k / kStepsPerHalf) * (BN / 2) + (k % kStepsPerHalf) * 8,
+    umma_ts_w(o_tmem, p_tmem + (k / kStepsPerHalf) * (BN / 2) + (k % kStepsPerHalf) * 8,
             desc_add(v_desc, k * kKeyStep), IDESC, (accumulate | k) ? 1u : 0u);
 }
 
@@ -285,72 +286,73 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp == kWarpMma) {
-    // ------------------------------------------------------------ UMMA issuer (one thread)
-    if (lane == 0) {
+    // ------------------------------------------------------------ UMMA issuer (whole warp;
+    // elect.sync picks the one lane that issues each tcgen05 instruction)
+    {
       const uint64_t dq0 = sdesc_sw(sQ, 16, C::kSbo, C::kLayout);
       const uint64_t dq1 = sdesc_sw(sQ + C::kQBytes, 16, C::kSbo, C::kLayout);
       const uint64_t dk0 = sdesc_sw(sK, 16, C::kSbo, C::kLayout);
       const uint64_t dv0 = sdesc_sw(sV, C::kKVChunkBytes, C::kSbo, C::kLayout);
       const uint32_t tS0 = tmem, tS1 = tmem + 128, tO0 = tmem + 256, tO1 = tmem + 384;
       const int n0 = w.nkv[0], n1 = w.nkv[1];
-      bool ok = mbar_wait(BAR(BAR_Q), 0, p.status, kDevTimeoutQ) &&
-                mbar_wait(BAR(BAR_KFULL + 0), 0, p.status, kDevTimeoutKV);
+      bool ok = warp_all(mbar_wait(BAR(BAR_Q), 0, p.status, kDevTimeoutQ)) &&
+                warp_all(mbar_wait(BAR(BAR_KFULL + 0), 0, p.status, kDevTimeoutKV));
       if (ok) {
         tc_fence_after();
         issue_qk<D, BN, BF16>(tS0, dq0, dk0);
-        umma_commit(BAR(BAR_SFULL + 0));
+        umma_commit_w(BAR(BAR_SFULL + 0));
         if (n1 > 0) {
           issue_qk<D, BN, BF16>(tS1, dq1, dk0);
-          umma_commit(BAR(BAR_SFULL + 1));
+          umma_commit_w(BAR(BAR_SFULL + 1));
         }
-        umma_commit(BAR(BAR_KEMPTY + 0));
+        umma_commit_w(BAR(BAR_KEMPTY + 0));
       }
       for (int j = 0; ok && j < nmax; ++j) {
         const int vs = j % VST;
         const int ks1 = (j + 1) % KST;
         const uint64_t dvj = dv0 + static_cast<uint64_t>((vs * C::kKVBytes) >> 4);
         const uint64_t dkn = dk0 + static_cast<uint64_t>((ks1 * C::kKVBytes) >> 4);
-        if (!(ok = mbar_wait(BAR(BAR_VFULL + vs), (j / VST) & 1, p.status, kDevTimeoutKV))) break;
+        if (!(ok = warp_all(mbar_wait(BAR(BAR_VFULL + vs), (j / VST) & 1, p.status, kDevTimeoutKV)))) break;
         bool k_ready = false;
         bool issued_s = false;
         // tile 0
         if (j < n0) {
-          if (!(ok = mbar_wait(BAR(BAR_PFULL + 0), j & 1, p.status, kDevTimeoutP))) break;
+          if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULL + 0), j & 1, p.status, kDevTimeoutP)))) break;
           tc_fence_after();
           issue_pv<D, BN, BF16>(tO0, tS0, dvj, j > 0 ? 1u : 0u);
           if (j + 1 == n0) {
-            umma_commit(BAR(BAR_OFULL + 0));
+            umma_commit_w(BAR(BAR_OFULL + 0));
           } else {
-            if (!(ok = mbar_wait(BAR(BAR_KFULL + ks1), ((j + 1) / KST) & 1, p.status, kDevTimeoutKV))) break;
+            if (!(ok = warp_all(mbar_wait(BAR(BAR_KFULL + ks1), ((j + 1) / KST) & 1, p.status, kDevTimeoutKV)))) break;
             tc_fence_after();
             k_ready = true;
             issue_qk<D, BN, BF16>(tS0, dq0, dkn);
-            umma_commit(BAR(BAR_SFULL + 0));
+            umma_commit_w(BAR(BAR_SFULL + 0));
             issued_s = true;
           }
         }
         // tile 1
         if (j < n1) {
-          if (!(ok = mbar_wait(BAR(BAR_PFULL + 1), j & 1, p.status, kDevTimeoutP))) break;
+          if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULL + 1), j & 1, p.status, kDevTimeoutP)))) break;
           tc_fence_after();
           issue_pv<D, BN, BF16>(tO1, tS1, dvj, j > 0 ? 1u : 0u);
           if (j + 1 == n1) {
-            umma_commit(BAR(BAR_OFULL + 1));
+            umma_commit_w(BAR(BAR_OFULL + 1));
           } else {
             if (!k_ready) {
-              if (!(ok = mbar_wait(BAR(BAR_KFULL + ks1), ((j + 1) / KST) & 1, p.status, kDevTimeoutKV))) break;
+              if (!(ok = warp_all(mbar_wait(BAR(BAR_KFULL + ks1), ((j + 1) / KST) & 1, p.status, kDevTimeoutKV)))) break;
               tc_fence_after();
             }
             issue_qk<D, BN, BF16>(tS1, dq1, dkn);
-            umma_commit(BAR(BAR_SFULL + 1));
+            umma_commit_w(BAR(BAR_SFULL + 1));
             issued_s = true;
           }
         }
-        if (issued_s) umma_commit(BAR(BAR_KEMPTY + ks1));  // K(j+1) read by every tile that needs it
-        umma_commit(BAR(BAR_VEMPTY + vs));                 // V(j) read by every tile that needs it
+        if (issued_s) umma_commit_w(BAR(BAR_KEMPTY + ks1));  // K(j+1) read by every tile that needs it
+        umma_commit_w(BAR(BAR_VEMPTY + vs));                 // V(j) read by every tile that needs it
       }
-      // All MMAs issued by this thread must finish before TMEM is released.
-      umma_commit(BAR(BAR_DRAIN));
+      // All MMAs issued by this warp must finish before TMEM is released.
+      umma_commit_w(BAR(BAR_DRAIN));
       drain_wait(BAR(BAR_DRAIN), 0, p.status);
     }
     __syncwarp();
