@@ -91,6 +91,24 @@ __device__ __forceinline__ void exp2_row(const uint32_t* s, const float* neg_m, 
   }
 }
 
+// P = 2^(s * scale - lse) for kN values with a per-value lse (read as float4 from shared memory,
+// so each (x, y) / (z, w) half is a ready register pair): y = lse - s * scale in one packed FMA and
+// 2^(-y), so no per-value negation is needed.
+template <int kN>
+__device__ __forceinline__ void exp2_row_lse(const uint32_t* s, const float* lse, float scale, float* out) {
+  const uint64_t nscale2 = f2(-scale, -scale);
+#pragma unroll
+  for (int c = 0; c < kN; c += 4) {
+    const float4 l4 = *reinterpret_cast<const float4*>(lse + c);
+    const uint64_t y0 = ffma2(f2u(s[c], s[c + 1]), nscale2, f2(l4.x, l4.y));
+    const uint64_t y1 = ffma2(f2u(s[c + 2], s[c + 3]), nscale2, f2(l4.z, l4.w));
+    out[c] = ex2_neg_approx(f2lo(y0));
+    out[c + 1] = ex2_neg_approx(f2hi(y0));
+    out[c + 2] = ex2_neg_approx(f2lo(y1));
+    out[c + 3] = ex2_neg_approx(f2hi(y1));
+  }
+}
+
 // Store one 32-column fp32 chunk of an accumulator row as 16-bit values (64 bytes).
 template <bool BF16>
 __device__ __forceinline__ void store_row_chunk(uint8_t* dst, const uint32_t (&v)[32], float scale) {
@@ -430,7 +448,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (ok) {
       tc_fence_after();
       uint8_t* orow = reinterpret_cast<uint8_t*>(p.dq) + ridx * (D * 2);
-#pragma unroll 1
       if constexpr (D >= 64) {
         for (int c = w * (D / 64); c < (w + 1) * (D / 64); ++c) {  // 32-column chunks
           uint32_t v[32];
@@ -652,18 +669,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tmem_ld_wait(sv[1]);
       const float* lse = reinterpret_cast<const float*>(sm.ptr + C::kOffLse + qs * C::kStat) + 64 * w;
       const float* del = reinterpret_cast<const float*>(sm.ptr + C::kOffDelta + os * C::kStat) + 64 * w;
-      float neg_lse[64];
-#pragma unroll
-      for (int c = 0; c < 64; c += 4) {
-        const float4 l4 = *reinterpret_cast<const float4*>(lse + c);
-        neg_lse[c] = -l4.x;
-        neg_lse[c + 1] = -l4.y;
-        neg_lse[c + 2] = -l4.z;
-        neg_lse[c + 3] = -l4.w;
-      }
       float pr[64];
-      exp2_row<32>(sv[0], neg_lse, scale, pr);
-      exp2_row<32>(sv[1], neg_lse + 32, scale, pr + 32);
+      exp2_row_lse<32>(sv[0], lse, scale, pr);
+      exp2_row_lse<32>(sv[1], lse + 32, scale, pr + 32);
       const int q0 = it * kBT + 64 * w;
       if (key > q0 || q0 + 64 > p.S) {  // some query of these 64 precedes the key, or lies past S
 #pragma unroll
@@ -705,9 +713,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             d4.w = q0 + c + 3 < p.S ? d4.w : 0.f;
           }
           const uint64_t a = fmul2(f2(pr[c], pr[c + 1]),
-                                   fadd2(f2u(dp[h2][4 * c4], dp[h2][4 * c4 + 1]), f2(-d4.x, -d4.y)));
+                                   fsub2(f2u(dp[h2][4 * c4], dp[h2][4 * c4 + 1]), f2(d4.x, d4.y)));
           const uint64_t bb = fmul2(f2(pr[c + 2], pr[c + 3]),
-                                    fadd2(f2u(dp[h2][4 * c4 + 2], dp[h2][4 * c4 + 3]), f2(-d4.z, -d4.w)));
+                                    fsub2(f2u(dp[h2][4 * c4 + 2], dp[h2][4 * c4 + 3]), f2(d4.z, d4.w)));
           pk[2 * c4] = pack2<BF16>(f2lo(a), f2hi(a));
           pk[2 * c4 + 1] = pack2<BF16>(f2lo(bb), f2hi(bb));
         }
