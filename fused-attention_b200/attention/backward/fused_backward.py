@@ -55,7 +55,7 @@ def _forward(q, k, v, tile_m, tile_n, out=None):
     B, H, N, D = q.shape
     o = torch.empty_like(q) if out is None else out
     lse = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
-    _native().fwd(q, k, v, o, lse, tile_m, tile_n)
+    _native().fwd(q, k, v, o, lse, tile_m, _native().FWD_KV_TILE)  # tile_n: divisibility rule only
     return o, lse
 
 
