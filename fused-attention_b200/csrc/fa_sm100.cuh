@@ -176,7 +176,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 }
 
 // 3-D tiled load: coordinates (x = head-dim column, y = sequence row, z = batch*head).
-// x is always a multiple of 64 elements here, i.e. 128-byte aligned.
+// x is always a multiple of the 32- or 64-column swizzle chunk here, i.e. 64- or 128-byte aligned.
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int x, int y, int z, uint64_t policy) {
   asm volatile(
