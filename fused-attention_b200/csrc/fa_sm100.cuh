@@ -276,38 +276,15 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool a
 }
 
 // ---------------------------------------------------------------- tcgen05: MMA issue
-// D[tmem] (+)= A[smem desc] * B[smem desc]^T   (one elected thread issues)
-__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                        uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
-}
-
-// D[tmem] (+)= A[tmem] * B[smem desc]   (A read from TMEM, K-major, 2 x 16-bit per column)
-__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                        uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
-}
-
-// Arrive (once) on an mbarrier when every tcgen05 op previously issued by this thread is done.
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-      : "memory");
-}
-
-// Warp-wide forms of the three calls above: the whole warp executes them with the same
-// (warp-uniform) operands and elect.sync lets exactly one lane, always the lowest, issue the
-// tcgen05 instruction, so commits track that lane's MMAs.  Descriptor arithmetic done by the
-// whole warp stays on the uniform datapath: a one-lane issue loop measured 75.5 cycles per
-// 128x128x16 UMMA with 16 busy warps on the SM, the warp-wide loop 64.8 (the UMMA's own rate).
+// UMMA issue and commit, called by a whole warp with the same (warp-uniform) operands:
+// elect.sync lets exactly one lane, always the lowest, issue the tcgen05 instruction, so every
+// commit tracks that lane's MMAs.
+//   umma_ss_w:     D[tmem] (+)= A[smem desc] * B[smem desc]^T
+//   umma_ts_w:     D[tmem] (+)= A[tmem] * B[smem desc]  (A K-major, 2 x 16-bit per TMEM column)
+//   umma_commit_w: arrive once on an mbarrier when every tcgen05 op issued so far is done.
+// Descriptor arithmetic done by the whole warp stays on the uniform datapath: a loop in which one
+// lane computed descriptors and issued measured 75.5 cycles per 128x128x16 UMMA with 16 busy
+// warps on the SM, the warp-wide loop 64.8 (the UMMA's own rate).
 __device__ __forceinline__ void umma_ss_w(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                           uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -406,12 +383,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
 __device__ __forceinline__ float ex2_neg_approx(float x) {
   float y;
   asm("{\n\t.reg .f32 t;\n\tneg.f32 t, %1;\n\tex2.approx.ftz.f32 %0, t;\n\t}" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ float lg2_approx(float x) {
-  float y;
-  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
