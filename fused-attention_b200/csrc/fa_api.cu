@@ -3,6 +3,7 @@
 // Host-side duties: argument validation (synchronous, before anything is enqueued), TMA tensor
 // map encoding through the driver entry point (no link-time libcuda dependency), work-grid
 // sizing, and the launch on the caller's stream.  Nothing here allocates device memory.
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -63,16 +64,20 @@ int make_map(CUtensorMap* m, const void* ptr, int bh, int S, int D, int dtype, i
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int check_device() {
-  static int cached[64];  // 0 unknown, 1 ok, 2 wrong arch
+  // Per-device answer, cached: 0 unknown, 1 ok, 2 wrong arch (threads may race to fill an entry;
+  // they all store the same value).
+  static std::atomic<int> cached[64];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e);
-  if (dev >= 0 && dev < 64 && cached[dev] != 0) return cached[dev] == 1 ? FA_OK : FA_ERR_DEVICE;
+  const bool slot = dev >= 0 && dev < 64;
+  const int known = slot ? cached[dev].load(std::memory_order_relaxed) : 0;
+  if (known != 0) return known == 1 ? FA_OK : FA_ERR_DEVICE;
   int major = 0;
   e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
   if (e != cudaSuccess) return cuda_fail(e);
   const int ok = (major == 10) ? 1 : 2;
-  if (dev >= 0 && dev < 64) cached[dev] = ok;
+  if (slot) cached[dev].store(ok, std::memory_order_relaxed);
   return ok == 1 ? FA_OK : FA_ERR_DEVICE;
 }
 
