@@ -31,6 +31,7 @@ FA_ERR_ALIGNMENT = 3
 FA_ERR_CUDA = 4
 FA_ERR_DRIVER = 5
 FA_ERR_DEVICE = 6
+FA_ERR_TOO_LARGE = 7
 
 # exported symbol -> (argtypes) ; every entry point returns int
 _VP, _I, _FP = ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p
@@ -86,8 +87,11 @@ def status_tensor(device):
         idx = torch.cuda.current_device()
     st = _status.get(idx)
     if st is None:
-        st = torch.zeros(4, dtype=torch.int32, device=f"cuda:{idx}")
-        _status[idx] = st
+        with _lock:
+            st = _status.get(idx)
+            if st is None:
+                st = torch.zeros(4, dtype=torch.int32, device=f"cuda:{idx}")
+                _status[idx] = st
     return st
 
 
@@ -108,11 +112,9 @@ def _raise(rc, what):
     msg = lib.fa_strerror(rc).decode()
     if rc == FA_ERR_CUDA:
         msg += ": " + lib.fa_last_cuda_error().decode()
-    if rc in (FA_ERR_INVALID_ARG,):
-        raise ValueError(f"{what}: {msg}")
-    if rc in (FA_ERR_UNSUPPORTED, FA_ERR_ALIGNMENT):
-        raise ValueError(f"{what}: {msg}")
-    raise RuntimeError(f"{what}: {msg}")
+    if rc in (FA_ERR_INVALID_ARG, FA_ERR_UNSUPPORTED, FA_ERR_ALIGNMENT, FA_ERR_TOO_LARGE):
+        raise ValueError(f"{what}: {msg}")  # the caller's arguments
+    raise RuntimeError(f"{what}: {msg}")  # CUDA, driver or device
 
 
 def _ptr(t):

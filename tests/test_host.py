@@ -46,6 +46,22 @@ def test_strerror_covers_codes():
     assert lib.fa_strerror(99).decode() == "unknown error code"
 
 
+def test_error_codes_match_the_header_and_map_to_python_exceptions():
+    """The binding's FA_ERR_* values are the header's; argument errors raise ValueError, CUDA /
+    driver / device errors RuntimeError, each with the library's message."""
+    nat = _native()
+    text = open(HEADER).read()
+    codes = {m.group(1): int(m.group(2)) for m in re.finditer(r"\b(FA_(?:OK|ERR_\w+))\s*=\s*(\d+)", text)}
+    assert codes and all(getattr(nat, name) == value for name, value in codes.items()), codes
+    lib = nat.load()
+    for name in ("FA_ERR_INVALID_ARG", "FA_ERR_UNSUPPORTED", "FA_ERR_ALIGNMENT", "FA_ERR_TOO_LARGE"):
+        with pytest.raises(ValueError, match=re.escape(lib.fa_strerror(codes[name]).decode())):
+            nat._raise(codes[name], "call")
+    for name in ("FA_ERR_DRIVER", "FA_ERR_DEVICE"):
+        with pytest.raises(RuntimeError, match=re.escape(lib.fa_strerror(codes[name]).decode())):
+            nat._raise(codes[name], "call")
+
+
 def _fwd_rc(**kw):
     lib = _native().load()
     args = dict(q=8, k=8, v=8, o=8, lse=None, B=1, H=8, H_kv=8, S=128, D=64, dtype=0, tm=64, tn=64,
