@@ -16,7 +16,6 @@ Extensions over the reference (documented gaps it leaves open): bfloat16 as well
 GQA/MQA (k, v with H_kv heads dividing H) in the backward too.
 """
 import importlib.util
-import math
 import os
 import sys
 
