@@ -212,3 +212,13 @@ def test_bench_reference_arm_prints_the_contract_line():
     assert line["impl"] == "reference" and line["value"] > 0
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
+
+
+def test_bench_reference_arm_prints_only_on_rank_0():
+    """Under torchrun the reference arm runs on rank 0 alone; other ranks exit 0 without output."""
+    r = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference", "--gpus", "2",
+                        "--steps", "1", "--warmup", "0", "--seq", "256", "--dim", "64"], capture_output=True,
+                       text=True, timeout=600,
+                       env={**os.environ, "CUDA_VISIBLE_DEVICES": "", "RANK": "1", "LOCAL_RANK": "1", "WORLD_SIZE": "2"})
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.strip() == ""
