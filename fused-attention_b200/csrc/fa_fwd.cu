@@ -12,21 +12,26 @@
 //   mode 1: q-tile i of query heads (2p, 2p+1)      (even GQA groups: K/V tile shared)
 // Grid order: bands of up to 16 work units, every unit's heaviest tile pair first inside a band
 // (see band_order), so the grid ends with its shortest CTAs.
-// Warp roles (640 threads):
-//   warps 0-15  four softmax warpgroups: warpgroup g serves query tile t = g / 2 and key-column
-//               half h = g % 2 (one TMEM lane = one query row per thread, BN/2 columns); the two
-//               halves of a row exchange partial maxima (and, at the end, partial sums) through
-//               shared memory behind one named barrier per tile
-//   warp 16     TMA producer: Q tiles once, then the K ring (K(j) is freed once every tile's
+// Warp roles (384 threads):
+//   warps 0-3   softmax warpgroup of query tile 0: one thread = one query row = one TMEM lane,
+//               holding the row's whole K/V tile of scores in registers (no exchange between
+//               warpgroups, S read from TMEM once)
+//   warps 4-7   softmax warpgroup of query tile 1
+//   warp 8      TMA producer: Q tiles once, then the K ring (K(j) is freed once every tile's
 //               Q K^T has read it, well before V(j) is freed, so K loads run ahead)
-//   warp 17     UMMA issuer (the whole warp computes descriptors, one elected lane issues):
+//   warp 9      UMMA issuer (the whole warp computes descriptors, one elected lane issues):
 //               S_t = Q_t K_j^T into TMEM, O_t += P_t V_j with P_t read from TMEM
-//   warp 18     TMA producer: the V ring
-//   warp 19     idle
+//   warp 10     TMA producer: the V ring
+//   warp 11     idle
 // TMEM (512 columns): S_0 | S_1 | O_0 | O_1, 128 columns each; P_t (16-bit) overwrites the first
-// half of each warpgroup's own S_t columns once the row has been read into registers.  The two
-// tiles ping-pong: while one tile's warpgroups turn S into P, the tensor core runs the other
-// tile's P V and next Q K^T.
+// BN/2 columns of S_t once the row is in registers.  The two tiles ping-pong: while one tile's
+// warpgroup turns S into P, the tensor core runs the other tile's P V and next Q K^T.  P is
+// published in two halves (keys [0, BN/2) and [BN/2, BN)), so the first half's P V runs while the
+// second half is exponentiated; on interior tiles the first half uses the running max, and the
+// new row max is computed alongside it instead of in front of it.
+// exp2: most of every row on the MUFU unit (ex2.approx), a fixed share as a degree-3 polynomial on
+// the FMA pipe (the MUFU unit alone needs as many cycles per tile as the tensor core: 16 results
+// per clock and SM against 8192 FLOP per clock).
 // O is rescaled in TMEM only when a row max grows by more than 2^8 (otherwise the stale max is
 // kept, which is exact because numerator and denominator use the same offset).
 #include "fa_internal.h"
@@ -35,14 +40,18 @@
 namespace fa {
 namespace {
 
-constexpr int kThreads = 640;
-constexpr int kSoftmaxWarps = 16;   // 4 warpgroups: tile t = wg / 2, column half h = wg % 2
-constexpr int kWarpProducerK = 16;  // Q tiles, then the K ring
-constexpr int kWarpMma = 17;
-constexpr int kWarpProducerV = 18;  // the V ring
+constexpr int kThreads = 384;
+constexpr int kSoftmaxWarps = 8;    // 2 warpgroups: tile t = warp / 4
+constexpr int kWarpProducerK = 8;   // Q tiles, then the K ring
+constexpr int kWarpMma = 9;
+constexpr int kWarpProducerV = 10;  // the V ring
 constexpr int kBM = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only if the max grows > 256x
+
+#ifndef FA_FWD_POLY_PAIRS
+#define FA_FWD_POLY_PAIRS 2  // of every 16 exp2 pairs, this many go to the FMA-pipe polynomial
+#endif
 
 template <int D, int BN>
 struct FwdCfg {
@@ -58,8 +67,7 @@ struct FwdCfg {
   static constexpr int kKVChunkBytes = BN * kSwBytes;
   static constexpr int kQBytes = kBM * D * 2;
   static constexpr int kKVBytes = BN * D * 2;       // one K (or V) tile
-  static constexpr int kXchBytes = 2 * 2 * 2 * kBM * 4 + 2 * 2 * kBM * 4;  // row-max (x2 parity) + row-sum
-  static constexpr int kBudget = 225 * 1024 - kXchBytes;
+  static constexpr int kBudget = 225 * 1024;
   static constexpr int kSlots = (kBudget - 2 * kQBytes) / kKVBytes;  // K + V ring slots that fit
   static constexpr int kVStages = (kSlots / 2) > 4 ? 4 : (kSlots / 2);
   static constexpr int kKStages = (kSlots - kVStages) > 4 ? 4 : (kSlots - kVStages);
@@ -67,8 +75,7 @@ struct FwdCfg {
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = 2 * kQBytes;
   static constexpr int kOffV = kOffK + kKStages * kKVBytes;
-  static constexpr int kOffXch = kOffV + kVStages * kKVBytes;
-  static constexpr int kOffBar = kOffXch + kXchBytes;
+  static constexpr int kOffBar = kOffV + kVStages * kKVBytes;
   static constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers + 1 KiB alignment slack
 };
 
@@ -80,10 +87,11 @@ enum : int {
   BAR_VFULL = 9,    // + V stage (4)
   BAR_VEMPTY = 13,  // + V stage (4)
   BAR_SFULL = 17,   // + tile (2)
-  BAR_PFULL = 19,   // + tile (2)
+  BAR_PFULLA = 19,  // + tile (2): P of the first half of the tile's keys is in TMEM
   BAR_OFULL = 21,   // + tile (2)
   BAR_DRAIN = 23,
-  BAR_COUNT = 24
+  BAR_PFULLB = 24,  // + tile (2): P of the second half
+  BAR_COUNT = 26
 };
 
 struct QTile {
@@ -134,19 +142,78 @@ __device__ __forceinline__ Work decode_work(const FwdParams& p, int item) {
   return w;
 }
 
-// P = 2^(S * scale - m) for 32 columns of one row: packed f32x2 math around MUFU ex2 (masked
-// entries, -inf, give exactly 0).  Every exp2 goes to the MUFU pipe: evaluating part of them as a
-// polynomial on the FMA pipe costs more instructions than it saves MUFU time, and the softmax is
-// bound by its instruction stream, not by MUFU throughput (measured 5-6 % slower forward).
-template <bool BF16>
+// 2^x for a pair of x <= 0 on the FMA pipe (no MUFU): x = n + f with n = round(x) (the 1.5 * 2^23
+// addition leaves n in the low mantissa bits) and f in [-1/2, 1/2]; 2^f by a degree-3 polynomial
+// fitted here to 2^f on [-1/2, 1/2] (relative-error least squares on Chebyshev nodes, reweighted
+// towards the worst points: max relative error 7.5e-5, below half an fp16 ulp); 2^n is added to
+// the result's exponent field.  x is clamped at -125 first: the polynomial's value lies in
+// [2^-1/2, 2^1/2], so its exponent field is 126 or 127 and stays >= 1 (a normal number) after
+// adding n >= -125.  Scores that far below the row maximum give at most 2^-124 instead of ~0,
+// below anything a 16-bit P or the fp32 row sum can resolve next to the row's largest term (1).
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
+  const float x0 = fmaxf(f2lo(x2), -125.f), x1 = fmaxf(f2hi(x2), -125.f);
+  const uint64_t xc = f2(x0, x1);
+  const uint64_t magic = f2(12582912.f, 12582912.f);
+  const uint64_t j = fadd2(xc, magic);
+  const uint64_t n = fsub2(j, magic);
+  const uint64_t f = fsub2(xc, n);
+  uint64_t p = ffma2(f2(0.05517164617776871f, 0.05517164617776871f), f,
+                     f2(0.24261116981506348f, 0.24261116981506348f));
+  p = ffma2(p, f, f2(0.6932609677314758f, 0.6932609677314758f));
+  p = ffma2(p, f, f2(0.9999280571937561f, 0.9999280571937561f));
+  const uint32_t lo = static_cast<uint32_t>(p) + (static_cast<uint32_t>(j) << 23);
+  const uint32_t hi = static_cast<uint32_t>(p >> 32) + (static_cast<uint32_t>(j >> 32) << 23);
+  return f2u(lo, hi);
+}
+
+// P = 2^(S * scale - m) for 32 columns of one row (masked entries, -inf, give 0; the polynomial
+// pairs are only used on tiles without masked entries).  kPoly of the 16 pairs, spread over the chunk, take the
+// polynomial; the rest go to MUFU ex2.
+template <bool BF16, int kPoly>
 __device__ __forceinline__ void softmax_chunk(const uint32_t (&r)[32], uint64_t scale2, uint64_t negm2,
                                               uint64_t (&sum2)[4], uint32_t (&pk)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const uint64_t x2 = ffma2(f2u(r[2 * i], r[2 * i + 1]), scale2, negm2);
-    const uint64_t p2 = f2(ex2_approx(f2lo(x2)), ex2_approx(f2hi(x2)));
+    // polynomial pairs spread evenly over the chunk (i = 3, 7, 11, 15 for four of them)
+    constexpr int kEvery = kPoly > 0 ? 16 / kPoly : 1;
+    const bool poly = kPoly > 0 && i % kEvery == kEvery - 1;
+    uint64_t p2;
+    if (poly)
+      p2 = exp2_poly2(x2);
+    else
+      p2 = f2(ex2_approx(f2lo(x2)), ex2_approx(f2hi(x2)));
     sum2[i & 3] = fadd2(sum2[i & 3], p2);
     pk[i] = pack2<BF16>(f2lo(p2), f2hi(p2));
+  }
+}
+
+// Row max over NCH 32-column chunks: eight independent chains of the three-input max of sm_100
+// (half the instructions of a two-input chain).
+template <int NCH>
+__device__ __forceinline__ float row_max(const uint32_t (&r)[NCH][32]) {
+  float m8[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) m8[u] = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int i = 0; i < 32; i += 2)
+      m8[(c * 16 + i / 2) % 8] = fmax3(m8[(c * 16 + i / 2) % 8], __uint_as_float(r[c][i]), __uint_as_float(r[c][i + 1]));
+  return fmaxf(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], fmax3(m8[5], m8[6], m8[7])));
+}
+
+// O row *= alpha in TMEM (D fp32 columns of this thread's lane).
+template <int D>
+__device__ __forceinline__ void rescale_o(uint32_t t_o, float alpha) {
+#pragma unroll 1
+  for (int c = 0; c < D / 32; ++c) {
+    uint32_t o[32];
+    tmem_ld32(t_o + c * 32, o);
+    tmem_ld_wait(o);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+    tmem_st32(t_o + c * 32, o);
   }
 }
 
@@ -164,20 +231,20 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint64_t q_desc, uint6
   }
 }
 
-// O += P V: P (16-bit) read from TMEM as the A operand, V MN-major in shared memory.  P is stored
-// in two halves, one per softmax warpgroup of the tile: keys [0, BN/2) packed at S columns
-// [0, BN/4), keys [BN/2, BN) at [BN/2, BN/2 + BN/4) (each warpgroup overwrites only the first
-// half of its own S columns, which it has already read).
+// O += P V over one half of the tile's keys (half = 0: keys [0, BN/2), 1: [BN/2, BN)): P (16-bit,
+// keys in order, two per TMEM column) read from the first BN/2 columns of S as the A operand, V
+// MN-major in shared memory.
 template <int D, int BN, bool BF16>
-__device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint64_t v_desc,
-                                         uint32_t accumulate) {
+__device__ __forceinline__ void issue_pv_half(uint32_t o_tmem, uint32_t p_tmem, uint64_t v_desc,
+                                              uint32_t accumulate, int half) {
   constexpr uint32_t IDESC = idesc_f16(BF16, kBM, D, false, true);
-  constexpr int kStepsPerHalf = BN / 32;
   constexpr int kKeyStep = 16 * FwdCfg<D, BN>::kSwBytes;  // 16 key rows of V
+  constexpr int kSteps = BN / 32;                          // 16-key UMMA steps per half
 #pragma unroll
-  for (int k = 0; k < BN / 16; ++k)
-    umma_ts_w(o_tmem, p_tmem + (k / kStepsPerHalf) * (BN / 2) + (k % kStepsPerHalf) * 8,
-            desc_add(v_desc, k * kKeyStep), IDESC, (accumulate | k) ? 1u : 0u);
+  for (int i = 0; i < kSteps; ++i) {
+    const int k = half * kSteps + i;
+    umma_ts_w(o_tmem, p_tmem + k * 8, desc_add(v_desc, k * kKeyStep), IDESC, (accumulate | k) ? 1u : 0u);
+  }
 }
 
 template <int D, int BN, bool BF16>
@@ -225,7 +292,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(BAR(BAR_SFULL + t), 1);
-      mbar_init(BAR(BAR_PFULL + t), 256);
+      mbar_init(BAR(BAR_PFULLA + t), 128);
+      mbar_init(BAR(BAR_PFULLB + t), 128);
       mbar_init(BAR(BAR_OFULL + t), 1);
     }
     mbar_init(BAR(BAR_DRAIN), 1);
@@ -317,9 +385,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool issued_s = false;
         // tile 0
         if (j < n0) {
-          if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULL + 0), j & 1, p.status, kDevTimeoutP)))) break;
+          if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULLA + 0), j & 1, p.status, kDevTimeoutP)))) break;
           tc_fence_after();
-          issue_pv<D, BN, BF16>(tO0, tS0, dvj, j > 0 ? 1u : 0u);
+          issue_pv_half<D, BN, BF16>(tO0, tS0, dvj, j > 0 ? 1u : 0u, 0);
+          if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULLB + 0), j & 1, p.status, kDevTimeoutP)))) break;
+          tc_fence_after();
+          issue_pv_half<D, BN, BF16>(tO0, tS0, dvj, 1u, 1);
           if (j + 1 == n0) {
             umma_commit_w(BAR(BAR_OFULL + 0));
           } else {
@@ -333,9 +404,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // tile 1
         if (j < n1) {
-          if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULL + 1), j & 1, p.status, kDevTimeoutP)))) break;
+          if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULLA + 1), j & 1, p.status, kDevTimeoutP)))) break;
           tc_fence_after();
-          issue_pv<D, BN, BF16>(tO1, tS1, dvj, j > 0 ? 1u : 0u);
+          issue_pv_half<D, BN, BF16>(tO1, tS1, dvj, j > 0 ? 1u : 0u, 0);
+          if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULLB + 1), j & 1, p.status, kDevTimeoutP)))) break;
+          tc_fence_after();
+          issue_pv_half<D, BN, BF16>(tO1, tS1, dvj, 1u, 1);
           if (j + 1 == n1) {
             umma_commit_w(BAR(BAR_OFULL + 1));
           } else {
@@ -359,174 +433,134 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   } else {
     // ------------------------------------------------------------ softmax / epilogue
-    // warpgroup g = warp / 4: tile t = g / 2, column half h = g % 2.  A thread owns one row
-    // (TMEM lane) and BN/2 columns; the two halves of a row exchange their partial maxima (and,
-    // at the end, their partial sums) through shared memory behind a named barrier per tile.
-    const int g = warp / 4;
-    const int t = g / 2, h = g % 2;
+    // warpgroup t serves query tile t; a thread owns one row (TMEM lane) and its BN scores.
+    const int t = warp / 4;
     if (t < w.ntiles) {
-      constexpr int HC = BN / 2;  // columns per half
+      constexpr int NCH = BN / 32;  // 32-column chunks of a row
       const QTile tile = w.t[t];
       const int nkv = w.nkv[t];
       const int wq = warp % 4;  // TMEM lane quarter this warp may access
       const int row = wq * 32 + lane;
       const int qrow = tile.qt * kBM + row;
       const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-      const uint32_t tS = tmem + t * 128 + lane_off + h * HC;
-      const uint32_t tO = tmem + 256 + t * 128 + lane_off + h * (D / 2);
-      float* xmax = reinterpret_cast<float*>(smem + C::kOffXch);           // [parity][tile][half][row]
-      float* xsum = xmax + 2 * 2 * 2 * kBM;                                // [tile][half][row]
-      const uint32_t named_bar = 1 + t;
+      const uint32_t tS = tmem + t * 128 + lane_off;
+      const uint32_t tO = tmem + 256 + t * 128 + lane_off;
       const float scale = p.scale_log2;
       float m_used = -INFINITY;
       float l = 0.f;
       bool ok = true;
       for (int j = 0; j < nkv; ++j) {
-        ok = warp_all(mbar_wait(BAR(BAR_SFULL + t), j & 1, p.status, kDevTimeoutS));
-        uint32_t r[HC / 32][32];
-        float mx_half = -INFINITY;
-        const int kbase = j * BN + h * HC;
-        const bool masked = kbase + HC - 1 > tile.qt * kBM || kbase + HC > p.S;
-        float* xm = xmax + ((j & 1) * 2 + t) * 2 * kBM;
-        if (ok) {
-          tc_fence_after();
+        if (!(ok = warp_all(mbar_wait(BAR(BAR_SFULL + t), j & 1, p.status, kDevTimeoutS)))) break;
+        tc_fence_after();
+        uint32_t r[NCH][32];
 #pragma unroll
-          for (int c = 0; c < HC / 32; ++c) tmem_ld32(tS + c * 32, r[c]);
+        for (int c = 0; c < NCH; ++c) tmem_ld32(tS + c * 32, r[c]);
 #pragma unroll
-          for (int c = 0; c < HC / 32; ++c) tmem_ld_wait(r[c]);
+        for (int c = 0; c < NCH; ++c) tmem_ld_wait(r[c]);
+        const int kbase = j * BN;
+        const bool masked = kbase + BN - 1 > tile.qt * kBM || kbase + BN > p.S;
+        const uint64_t scale2 = f2(scale, scale);
+        uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
+        float alpha = 1.f;
+        if (masked || j == 0) {
+          // Diagonal or ragged tile, or the row's first tile: the exact row max first, then P.
           if (masked) {
 #pragma unroll
-            for (int c = 0; c < HC / 32; ++c)
+            for (int c = 0; c < NCH; ++c)
 #pragma unroll
               for (int i = 0; i < 32; ++i) {
                 const int key = kbase + c * 32 + i;
                 if (key > qrow || key >= p.S) r[c][i] = __float_as_uint(-INFINITY);
               }
           }
-          // three-input max (sm_100): half the instructions of a two-input chain
-          float mx4[4];
+          const float mt = row_max<NCH>(r) * scale;
+          const bool upd = mt > m_used + kRescaleThreshold;
+          const float m_new = upd ? mt : m_used;
+          alpha = ex2_approx(m_used - m_new);
+          const uint64_t negm2 = f2(-m_new, -m_new);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) mx4[u] = -INFINITY;
-#pragma unroll
-          for (int c = 0; c < HC / 32; ++c)
-#pragma unroll
-            for (int i = 0; i < 32; i += 2)
-              mx4[(i / 2) % 4] = fmax3(mx4[(i / 2) % 4], __uint_as_float(r[c][i]), __uint_as_float(r[c][i + 1]));
-          mx_half = fmaxf(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3]);
-          // full row max: exchange with the other half (double-buffered by KV-step parity)
-          xm[h * kBM + row] = mx_half;
-        }
-        // every thread of the tile arrives here once per step; all leave together on failure
-        if (!named_bar_and(named_bar, 256, ok)) {
-          ok = false;
-          break;
-        }
-        const float mx = fmaxf(mx_half, xm[(1 - h) * kBM + row]);
-        const float mt = mx * scale;
-        const bool upd = mt > m_used + kRescaleThreshold;
-        const float m_new = upd ? mt : m_used;
-        const float alpha = ex2_approx(m_used - m_new);
-        const uint64_t scale2 = f2(scale, scale);
-        const uint64_t negm2 = f2(-m_new, -m_new);
-        uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
-        // exp pass: re-read each 32-column chunk from TMEM (keeps register pressure at one chunk)
-#pragma unroll
-        for (int c = 0; c < HC / 32; ++c) {
-          uint32_t rc[32];
-          tmem_ld32(tS + c * 32, rc);
-          tmem_ld_wait(rc);
-          if (masked) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int key = kbase + c * 32 + i;
-              if (key > qrow || key >= p.S) rc[i] = __float_as_uint(-INFINITY);
-            }
+          for (int c = 0; c < NCH; ++c) {
+            uint32_t pk[16];
+            softmax_chunk<BF16, 0>(r[c], scale2, negm2, sum2, pk);
+            tmem_st16(tS + c * 16, pk);
           }
-          uint32_t pk[16];
-          // Two call sites on purpose: diagonal and interior tiles get separately scheduled
-          // copies.  With one shared call site ptxas goes over the 96-register cap of this
-          // 640-thread block and spills (-Xptxas -v: 12-16 bytes for BN = 128).
-          if (masked)
-            softmax_chunk<BF16>(rc, scale2, negm2, sum2, pk);
-          else
-            softmax_chunk<BF16>(rc, scale2, negm2, sum2, pk);
-          tmem_st16(tS + c * 16, pk);
+          // Rescale the running O if any row's max moved (P V of tile j-1 is complete: it was
+          // issued before S_t(j), whose completion we waited for).
+          if (j > 0 && __any_sync(0xffffffffu, upd)) rescale_o<D>(tO, alpha);
+          m_used = m_new;
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(BAR(BAR_PFULLA + t));
+          mbar_arrive(BAR(BAR_PFULLB + t));
+        } else {
+          // Interior tile: P of the first half of the keys with the running max m_used while the
+          // new row max is computed alongside (off the S -> P critical path).  A row whose max
+          // rose by more than the threshold redoes that half with the new max and rescales O
+          // before anything is published; the second half then uses the settled max.
+          uint64_t negm2 = f2(-m_used, -m_used);
+#pragma unroll
+          for (int c = 0; c < NCH / 2; ++c) {
+            uint32_t pk[16];
+            softmax_chunk<BF16, FA_FWD_POLY_PAIRS>(r[c], scale2, negm2, sum2, pk);
+            tmem_st16(tS + c * 16, pk);
+          }
+          const float mt = row_max<NCH>(r) * scale;
+          const bool upd = mt > m_used + kRescaleThreshold;
+          if (__any_sync(0xffffffffu, upd)) {
+            const float m_new = upd ? mt : m_used;
+            alpha = ex2_approx(m_used - m_new);
+            negm2 = f2(-m_new, -m_new);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) sum2[u] = 0ull;
+#pragma unroll
+            for (int c = 0; c < NCH / 2; ++c) {
+              uint32_t pk[16];
+              softmax_chunk<BF16, 0>(r[c], scale2, negm2, sum2, pk);
+              tmem_st16(tS + c * 16, pk);
+            }
+            rescale_o<D>(tO, alpha);
+            m_used = m_new;
+          }
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(BAR(BAR_PFULLA + t));
+#pragma unroll
+          for (int c = NCH / 2; c < NCH; ++c) {
+            uint32_t pk[16];
+            softmax_chunk<BF16, FA_FWD_POLY_PAIRS>(r[c], scale2, negm2, sum2, pk);
+            tmem_st16(tS + c * 16, pk);
+          }
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(BAR(BAR_PFULLB + t));
         }
         const uint64_t s01 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
         l = l * alpha + (f2lo(s01) + f2hi(s01));
-        m_used = m_new;
-        // Rescale this half of the running O if any row's max moved (P V of tile j-1 is complete:
-        // it was issued before S_t(j), whose completion we waited for).
-        if (j > 0 && __any_sync(0xffffffffu, upd)) {
-          if constexpr (D >= 64) {
-#pragma unroll 1
-            for (int c = 0; c < D / 64; ++c) {
-              uint32_t o[32];
-              tmem_ld32(tO + c * 32, o);
-              tmem_ld_wait(o);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-              tmem_st32(tO + c * 32, o);
-            }
-          } else {  // D = 32: 16 columns per half
-            uint32_t o[16];
-            tmem_ld16(tO, o);
-            tmem_ld_wait16(o);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st16(tO, o);
-          }
-        }
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(BAR(BAR_PFULL + t));
       }
-      // Row sum over both halves.  Every thread of the tile reaches this barrier, whether or not
-      // its pipeline waits succeeded, so the named-barrier count always matches.
-      xsum[(t * 2 + h) * kBM + row] = l;
-      named_bar_sync(named_bar, 256);
-      const float l_row = l + xsum[(t * 2 + 1 - h) * kBM + row];
       if (ok) ok = mbar_wait(BAR(BAR_OFULL + t), 0, p.status, kDevTimeoutO);
       ok = warp_all(ok);
       if (ok) {
         tc_fence_after();
-        const float inv_l = 1.0f / l_row;
-        uint8_t* orow = reinterpret_cast<uint8_t*>(p.o) +
-                        (static_cast<size_t>(tile.bh) * p.S + qrow) * (D * 2) + h * D;
-        if constexpr (D >= 64) {
+        const float inv_l = 1.0f / l;
+        uint8_t* orow = reinterpret_cast<uint8_t*>(p.o) + (static_cast<size_t>(tile.bh) * p.S + qrow) * (D * 2);
 #pragma unroll 1
-          for (int c = 0; c < D / 64; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tO + c * 32, o);
-            tmem_ld_wait(o);
-            uint32_t pk[16];
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_ld_wait(o);
+          uint32_t pk[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              pk[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l,
-                                  __uint_as_float(o[2 * i + 1]) * inv_l);
-            if (qrow < p.S) {
-              uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
-#pragma unroll
-              for (int v = 0; v < 4; ++v)
-                dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
-            }
-          }
-        } else {  // D = 32: 16 columns (32 bytes) per half
-          uint32_t o[16];
-          tmem_ld16(tO, o);
-          tmem_ld_wait16(o);
-          uint32_t pk[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
+          for (int i = 0; i < 16; ++i)
             pk[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
           if (qrow < p.S) {
-            uint4* dst = reinterpret_cast<uint4*>(orow);
-            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
           }
         }
-        if (h == 0 && p.lse != nullptr && qrow < p.S)
-          p.lse[static_cast<size_t>(tile.bh) * p.S + qrow] = m_used + log2f(l_row);
+        if (p.lse != nullptr && qrow < p.S)
+          p.lse[static_cast<size_t>(tile.bh) * p.S + qrow] = m_used + log2f(l);
       }
     }
   }
