@@ -12,14 +12,44 @@
 #include "fa_internal.h"
 
 namespace {
-
 thread_local char g_last_cuda_error[256] = "";
+}  // namespace
+
+namespace fa {
 
 int cuda_fail(cudaError_t e) {
   std::snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "%s: %s", cudaGetErrorName(e),
                 cudaGetErrorString(e));
+  // The error now lives in fa_last_cuda_error(); clear the runtime's (non-sticky) last-error
+  // state so that a host framework does not report it again at an unrelated later call.
+  (void)cudaGetLastError();
   return e == cudaErrorNotSupported ? FA_ERR_UNSUPPORTED : FA_ERR_CUDA;
 }
+
+int check_device() {
+  // Per-device answer, cached: 0 unknown, 1 ok, 2 wrong arch (threads may race to fill an entry;
+  // they all store the same value).
+  static std::atomic<int> cached[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  const bool slot = dev >= 0 && dev < 64;
+  const int known = slot ? cached[dev].load(std::memory_order_relaxed) : 0;
+  if (known != 0) return known == 1 ? FA_OK : FA_ERR_DEVICE;
+  int major = 0;
+  e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  const int ok = (major == 10) ? 1 : 2;
+  if (slot) cached[dev].store(ok, std::memory_order_relaxed);
+  return ok == 1 ? FA_OK : FA_ERR_DEVICE;
+}
+
+}  // namespace fa
+
+namespace {
+
+using fa::check_device;
+using fa::cuda_fail;
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -62,24 +92,6 @@ int make_map(CUtensorMap* m, const void* ptr, int bh, int S, int D, int dtype, i
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
-int check_device() {
-  // Per-device answer, cached: 0 unknown, 1 ok, 2 wrong arch (threads may race to fill an entry;
-  // they all store the same value).
-  static std::atomic<int> cached[64];
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e);
-  const bool slot = dev >= 0 && dev < 64;
-  const int known = slot ? cached[dev].load(std::memory_order_relaxed) : 0;
-  if (known != 0) return known == 1 ? FA_OK : FA_ERR_DEVICE;
-  int major = 0;
-  e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
-  if (e != cudaSuccess) return cuda_fail(e);
-  const int ok = (major == 10) ? 1 : 2;
-  if (slot) cached[dev].store(ok, std::memory_order_relaxed);
-  return ok == 1 ? FA_OK : FA_ERR_DEVICE;
-}
 
 // Argument checks that need no device: every entry point runs them (and its alignment checks)
 // before check_device(), so a bad argument is reported the same way with or without a GPU.

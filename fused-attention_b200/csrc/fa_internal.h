@@ -64,6 +64,13 @@ inline cudaError_t opt_in_smem(Kernel kernel, int bytes, std::atomic<bool> (&don
   return e;
 }
 
+// Host helpers of the C-ABI layer (fa_api.cu), shared with fa_noalloc.cu.
+// cuda_fail: records `e` as the text fa_last_cuda_error() returns and maps it to an FA_ERR_* code.
+// check_device: FA_OK if the current device is compute capability 10.x, else FA_ERR_DEVICE (or the
+// FA_ERR_* code of a failed runtime query).
+int cuda_fail(cudaError_t e);
+int check_device();
+
 // Launchers implemented in the kernel translation units.  They return a cudaError_t.
 cudaError_t launch_fwd(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
                        const FwdParams& p, int D, int block_n, bool bf16, cudaStream_t stream);

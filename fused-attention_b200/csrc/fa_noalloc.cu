@@ -9,10 +9,15 @@
 // library's device code is loaded on a GPU and held by every GPU that loads the library until the
 // process exits.  The caller still passes all inputs and outputs.
 //
-// Set-up: the first call on a device (with that device current) resolves the array's device
-// address with cudaGetSymbolAddress and caches it; make that first call before any stream
-// capture on the device.  The host-side name of the array is only a stand-in and is never passed
-// to a kernel.
+// Address of the array: the host-side name of the array is only a stand-in and is never passed to
+// a kernel.  Every call made outside stream capture looks up the array's device address in the
+// current CUDA context (cudaGetSymbolAddress, after the device check) and remembers it for that
+// context; a call made while its stream is being captured uses the address remembered for the
+// current context, so the first call in a context must come before any stream capture there (a
+// captured call without one fails with FA_ERR_CUDA).  Because every uncaptured call looks the
+// address up again, a context created after cudaDeviceReset, or a different context on the same
+// device (a driver-API caller with its own cuCtxCreate), never runs with another context's
+// address once it has made one uncaptured call.
 //
 // Sharing: every call on a device uses the same array and leaves its delta in it.  Nothing needs
 // clearing first, because the preprocess kernel writes every row the two gradient kernels read.
@@ -21,27 +26,64 @@
 #include <mutex>
 
 #include "../../include/fa_sm100.h"
+#include "fa_internal.h"
 
 namespace {
 
 __device__ __align__(256) float g_delta_scratch[FA_NOALLOC_MAX_ROWS];
 
-constexpr int kMaxDevices = 64;
-float* g_scratch_ptr[kMaxDevices];
-std::mutex g_scratch_mu;
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
 
-// Device address of the scratch array on the current device (resolved once per device).
-int scratch_for_current_device(float** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return FA_ERR_CUDA;
-  if (dev < 0 || dev >= kMaxDevices) return FA_ERR_DEVICE;
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_ptr[dev] == nullptr) {
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_delta_scratch) != cudaSuccess || p == nullptr) return FA_ERR_CUDA;
-    g_scratch_ptr[dev] = static_cast<float*>(p);
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
+
+// Scratch addresses remembered per CUDA context (filled by uncaptured calls, read by captured ones).
+constexpr int kCacheSlots = 64;
+struct ScratchEntry {
+  CUcontext ctx;
+  float* ptr;
+};
+ScratchEntry g_cache[kCacheSlots];
+int g_cache_next = 0;
+std::mutex g_cache_mu;
+
+int scratch_for_current_context(cudaStream_t stream, float** out) {
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(stream, &capture);
+  if (e != cudaSuccess) return fa::cuda_fail(e);
+  CtxGetCurrentFn get_ctx = ctx_get_current_fn();
+  CUcontext ctx = nullptr;
+  if (get_ctx == nullptr || get_ctx(&ctx) != CUDA_SUCCESS || ctx == nullptr) return FA_ERR_DRIVER;
+  std::lock_guard<std::mutex> lock(g_cache_mu);
+  int slot = -1;
+  for (int i = 0; i < kCacheSlots; ++i)
+    if (g_cache[i].ctx == ctx) slot = i;
+  if (capture != cudaStreamCaptureStatusNone) {
+    if (slot < 0) return fa::cuda_fail(cudaErrorStreamCaptureUnsupported);
+    *out = g_cache[slot].ptr;
+    return FA_OK;
   }
-  *out = g_scratch_ptr[dev];
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_delta_scratch);
+  if (e != cudaSuccess) return fa::cuda_fail(e);
+  if (p == nullptr) return fa::cuda_fail(cudaErrorInvalidSymbol);
+  if (slot < 0) {
+    slot = g_cache_next;
+    g_cache_next = (g_cache_next + 1) % kCacheSlots;
+  }
+  g_cache[slot] = {ctx, static_cast<float*>(p)};
+  *out = static_cast<float*>(p);
   return FA_OK;
 }
 
@@ -64,8 +106,12 @@ extern "C" int fa_bwd_noalloc(const void* q, const void* k, const void* v, const
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(dO) ||
       !aligned16(lse) || !aligned16(dq) || !aligned16(dk) || !aligned16(dv))
     return FA_ERR_ALIGNMENT;
+  // The device check comes first: on a GPU that is not sm_100 the symbol lookup would fail with
+  // a runtime error instead of the FA_ERR_DEVICE every other entry point returns.
+  int rc = fa::check_device();
+  if (rc != FA_OK) return rc;
   float* delta = nullptr;
-  int rc = scratch_for_current_device(&delta);
+  rc = scratch_for_current_context(static_cast<cudaStream_t>(stream), &delta);
   if (rc != FA_OK) return rc;
   rc = fa_bwd_preprocess(o, dO, delta, B, H, S, D, dtype, dev_status, stream);
   if (rc != FA_OK) return rc;

@@ -95,8 +95,11 @@ FA_API int fa_bwd_dq(const void* q, const void* k, const void* v, const void* dO
  * reference.  Same tensors and rules as the three calls above, minus `delta`: the float32 delta
  * scratch lives in a static device array of FA_NOALLOC_MAX_ROWS rows that every GPU loading the
  * library holds until exit; larger problems (B*H*S > FA_NOALLOC_MAX_ROWS) return
- * FA_ERR_TOO_LARGE.  This call allocates nothing (no cudaMalloc/cudaFree).  Its first call on a
- * device resolves the array's address on that device (make it before any stream capture there).
+ * FA_ERR_TOO_LARGE.  This call allocates nothing (no cudaMalloc/cudaFree).  A call made outside
+ * stream capture looks up the array's address in the current CUDA context and remembers it; a
+ * call made while its stream is captured uses the address remembered for the current context, so
+ * make the first call in a context before any stream capture there (otherwise FA_ERR_CUDA).  After
+ * cudaDeviceReset the next uncaptured call looks the address up again.
  * All calls on a device share the array: calls that overlap on the GPU race and must not be
  * issued; sequential calls need no clearing (every row is rewritten before it is read). */
 FA_API int fa_bwd_noalloc(const void* q, const void* k, const void* v, const void* o,
