@@ -18,11 +18,14 @@ import torch
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libfa_sm100.so")
 ABI_VERSION = 1
 
-# K/V tile of the forward kernel that the drop-in wrappers launch.  128 keys per tile measured
-# faster than 64 at every size on B200 (15-18 % at N = 8192, equal at N <= 512), so the wrappers
-# keep the reference's tile_m / tile_n only for its divisibility contract and always launch this
-# tile; the C ABI (and fwd() below) still takes tile_n explicitly.
-FWD_KV_TILE = 128
+
+
+def kv_tile(tile_n):
+    """K/V tile (keys per tile) of the forward kernel for the reference's `tile_n` knob: the sm_100a
+    forward has 64- and 128-key variants, so tile_n <= 64 runs the 64-key tile and larger tile_n
+    the 128-key tile (the faster one on B200: 15-18 % at N = 8192).  The query side always runs
+    128-row tcgen05 tiles, so tile_m takes part only in the caller's divisibility rule."""
+    return 64 if int(tile_n) <= 64 else 128
 
 FA_OK = 0
 FA_ERR_INVALID_ARG = 1

@@ -54,7 +54,8 @@ def _forward(q, k, v, tile_m, tile_n, out=None):
     B, H, N, D = q.shape
     o = torch.empty_like(q) if out is None else out
     lse = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
-    _native().fwd(q, k, v, o, lse, tile_m, _native().FWD_KV_TILE)  # tile_n: divisibility rule only
+    nat = _native()
+    nat.fwd(q, k, v, o, lse, tile_m, nat.kv_tile(tile_n))  # the backward kernels run 128 x 128 tiles
     return o, lse
 
 

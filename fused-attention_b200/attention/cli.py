@@ -30,20 +30,34 @@ def parse_args(argv, description):
     return p.parse_args(argv)
 
 
+class _Exit(Exception):
+    """Ends the CLI with `code` after printing `error: <message>` to stderr."""
+
+    def __init__(self, code, message):
+        super().__init__(message)
+        self.code = code
+
+
+_NPZ_KEYS = ("Q", "K", "V")
+
+
 def load_qkv(path, ValidationError):
-    """Load Q, K, V from an .npz file, raising ValidationError for missing or malformed files."""
+    """Q, K, V arrays of an .npz file; ValidationError (with the reference's messages) when the file
+    is absent, unreadable or lacks one of the three arrays."""
     try:
-        with np.load(path, allow_pickle=False) as data:
-            missing = [key for key in ("Q", "K", "V") if key not in data.files]
-            if missing:
-                raise ValidationError(f"{path} is missing array(s) {', '.join(missing)}; found {sorted(data.files)}")
-            return data["Q"], data["K"], data["V"]
+        archive = np.load(path, allow_pickle=False)
     except FileNotFoundError:
-        raise ValidationError(f"input file not found: {path}")
+        raise ValidationError(f"input file not found: {path}") from None
     except (OSError, ValueError) as e:
-        if isinstance(e, ValidationError):
-            raise
-        raise ValidationError(f"could not read {path} as .npz: {e}")
+        raise ValidationError(f"could not read {path} as .npz: {e}") from None
+    with archive:
+        absent = [name for name in _NPZ_KEYS if name not in archive.files]
+        if absent:
+            raise ValidationError(f"{path} is missing array(s) {', '.join(absent)}; found {sorted(archive.files)}")
+        try:
+            return tuple(archive[name] for name in _NPZ_KEYS)
+        except (OSError, ValueError) as e:
+            raise ValidationError(f"could not read {path} as .npz: {e}") from None
 
 
 def _to_torch(x):
@@ -62,40 +76,58 @@ def run(q, k, v, fn, block_m, block_n):
     return out.to(torch.float16).cpu().numpy()
 
 
-def main(argv, description, get_backend, validate_qkv, ValidationError):
-    args = parse_args(argv, description)
+def _inputs(args, validate_qkv, ValidationError):
+    """Loaded and validated Q, K, V; an invalid input ends the CLI with exit status 2."""
     try:
         q, k, v = load_qkv(args.input, ValidationError)
         validate_qkv(q, k, v, args.block_m, args.block_n)
     except ValidationError as e:
-        print(f"error: {e}", file=sys.stderr)
-        return EXIT_INVALID
-    if args.verbose:
-        print(f"Q{q.shape} K{k.shape} V{v.shape} backend={args.backend} "
-              f"block_m={args.block_m} block_n={args.block_n}", file=sys.stderr)
+        raise _Exit(EXIT_INVALID, str(e)) from None
+    return q, k, v
+
+
+def _runtime_message(backend, err):
+    """The message for a failure while resolving or running a backend (exit status 1)."""
+    if isinstance(err, NotImplementedError):
+        return str(err) or f"backend {backend!r} is not implemented yet"
+    if isinstance(err, ModuleNotFoundError):
+        return f"missing dependency '{err.name}'"
+    return f"{backend} backend failed: {type(err).__name__}: {err}"
+
+
+def _compute(args, get_backend, q, k, v):
+    """(output array, seconds).  The backend is looked up before any data moves to the GPU, so an
+    unavailable backend is reported without touching the device."""
     try:
-        fn = get_backend(args.backend)  # resolve first so unimplemented backends fail fast
+        fn = get_backend(args.backend)
         t0 = time.perf_counter()
         out = run(q, k, v, fn, args.block_m, args.block_n)
-        elapsed = time.perf_counter() - t0
-    except NotImplementedError as e:
-        print(f"error: {str(e) or f'backend {args.backend!r} is not implemented yet'}", file=sys.stderr)
-        return EXIT_RUNTIME
-    except ModuleNotFoundError as e:
-        print(f"error: missing dependency '{e.name}'", file=sys.stderr)
-        return EXIT_RUNTIME
-    except Exception as e:  # kernel/driver failures
-        print(f"error: {args.backend} backend failed: {type(e).__name__}: {e}", file=sys.stderr)
-        return EXIT_RUNTIME
+        return out, time.perf_counter() - t0
+    except Exception as e:
+        raise _Exit(EXIT_RUNTIME, _runtime_message(args.backend, e)) from None
+
+
+def _check_output(out, q, v):
+    """A wrongly shaped or non-finite result is a runtime failure (exit status 1)."""
     expected = q.shape[:3] + (v.shape[3],)
     if out.shape != expected:
-        print(f"error: backend returned shape {out.shape}, expected {expected}", file=sys.stderr)
-        return EXIT_RUNTIME
+        raise _Exit(EXIT_RUNTIME, f"backend returned shape {out.shape}, expected {expected}")
     if not np.isfinite(out).all():
-        print("error: output contains NaN or Inf", file=sys.stderr)
-        return EXIT_RUNTIME
+        raise _Exit(EXIT_RUNTIME, "output contains NaN or Inf")
+
+
+def main(argv, description, get_backend, validate_qkv, ValidationError):
+    args = parse_args(argv, description)
+    say = (lambda text: print(text, file=sys.stderr)) if args.verbose else (lambda text: None)
+    try:
+        q, k, v = _inputs(args, validate_qkv, ValidationError)
+        say(f"Q{q.shape} K{k.shape} V{v.shape} backend={args.backend} "
+            f"block_m={args.block_m} block_n={args.block_n}")
+        out, seconds = _compute(args, get_backend, q, k, v)
+        _check_output(out, q, v)
+    except _Exit as stop:
+        print(f"error: {stop}", file=sys.stderr)
+        return stop.code
     np.save(args.output, out.astype(OUTPUT_DTYPE, copy=False))
-    if args.verbose:
-        print(f"wrote {args.output} {out.shape} {OUTPUT_DTYPE.__name__} in {elapsed:.3f}s "
-              f"(includes transfer)", file=sys.stderr)
+    say(f"wrote {args.output} {out.shape} {OUTPUT_DTYPE.__name__} in {seconds:.3f}s (includes transfer)")
     return EXIT_OK

@@ -34,8 +34,9 @@ def fused_attention(q, k, v, tile_m=64, tile_n=64):
     """Causal softmax(q k^T / sqrt(D)) v for q, k, v of shape [B, H, N, D] (float16 or bfloat16).
 
     Raises ValueError if N is not divisible by tile_m and tile_n (as the reference does).
-    tile_m and tile_n (64 or 128) are the reference's tile knobs and keep its divisibility rule;
-    the sm_100a kernel always runs 128-row query tiles and 128-key K/V tiles (its fastest shape).
+    tile_n selects the kernel's K/V tile (64 keys for tile_n <= 64, else 128, the faster one); the
+    query side always runs 128-row tcgen05 tiles, so tile_m only takes part in the divisibility
+    rule.
     """
     B, H, N, D = q.shape
     if N % tile_m != 0 or N % tile_n != 0:
@@ -44,5 +45,6 @@ def fused_attention(q, k, v, tile_m=64, tile_n=64):
         raise ValueError(f"q, k, v must all be (B, H, N, D); got {tuple(q.shape)}, {tuple(k.shape)}, {tuple(v.shape)}")
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     O = torch.empty_like(q)
-    _native().fwd(q, k, v, O, None, tile_m, _native().FWD_KV_TILE)
+    nat = _native()
+    nat.fwd(q, k, v, O, None, tile_m, nat.kv_tile(tile_n))
     return O

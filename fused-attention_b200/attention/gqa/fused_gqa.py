@@ -29,8 +29,8 @@ def _native():
 def fused_gqa_attention(q, k, v, tile_m=64, tile_n=64):
     """Causal GQA attention: q [B, H, N, D], k and v [B, H_kv, N, D] with H_kv dividing H.
 
-    tile_m and tile_n keep the reference's divisibility rule; the kernel runs its own 128 x 128
-    tiles."""
+    tile_m and tile_n keep the reference's divisibility rule; tile_n also selects the kernel's K/V
+    tile (64 keys for tile_n <= 64, else 128) and the query side always runs 128-row tiles."""
     B, H, N, D = q.shape
     H_kv = k.shape[1]
     if tuple(k.shape) != (B, H_kv, N, D) or v.shape != k.shape or H % H_kv != 0:
@@ -39,5 +39,6 @@ def fused_gqa_attention(q, k, v, tile_m=64, tile_n=64):
         raise ValueError(f"N={N} must be divisible by tile_m={tile_m} and tile_n={tile_n}")
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     O = torch.empty_like(q)
-    _native().fwd(q, k, v, O, None, tile_m, _native().FWD_KV_TILE)
+    nat = _native()
+    nat.fwd(q, k, v, O, None, tile_m, nat.kv_tile(tile_n))
     return O

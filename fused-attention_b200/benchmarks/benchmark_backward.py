@@ -37,90 +37,121 @@ def naive_attention(q, k, v):
     return torch.softmax(s, dim=-1).to(q.dtype) @ v
 
 
-def event_ms(fn):
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    fn()
-    b.record()
-    torch.cuda.synchronize()
-    return a.elapsed_time(b)
+class Timings:
+    """CUDA-event timings of one implementation on one input set (fresh leaf copies of q, k, v)."""
+
+    def __init__(self, fn, q, k, v, do):
+        self.fn, self.do = fn, do
+        self.leaves = [t.detach().clone().requires_grad_(True) for t in (q, k, v)]
+
+    def _zero_grads(self):
+        for t in self.leaves:
+            t.grad = None
+
+    def _timed(self, body, setup=None):
+        """Device ms of body(); setup() (untimed) runs first and its result is passed on."""
+        arg = setup() if setup is not None else None
+        if setup is not None:
+            torch.cuda.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        body(arg)
+        stop.record()
+        stop.synchronize()
+        return start.elapsed_time(stop)
+
+    def step(self):
+        self._zero_grads()
+        self.fn(*self.leaves).backward(self.do)
+
+    def forward_ms(self, reps):
+        with torch.no_grad():
+            return statistics.median(self._timed(lambda _: self.fn(*self.leaves)) for _ in range(reps))
+
+    def backward_ms(self, reps):
+        def setup():
+            self._zero_grads()
+            return self.fn(*self.leaves)
+        return statistics.median(self._timed(lambda o: o.backward(self.do), setup) for _ in range(reps))
+
+    def step_ms(self, reps):
+        return statistics.median(self._timed(lambda _: self.step()) for _ in range(reps))
+
+    def peak_extra_mb(self):
+        """Peak device memory above the resident inputs while one forward + backward runs."""
+        self._zero_grads()
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        resident = torch.cuda.memory_allocated()
+        torch.cuda.reset_peak_memory_stats()
+        self.step()
+        torch.cuda.synchronize()
+        return (torch.cuda.max_memory_allocated() - resident) / float(1 << 20)
 
 
 def measure(fn, q, k, v, do, warmup, reps):
     """Median ms of forward, backward and forward + backward; peak extra MB of one fwd + bwd."""
-    q, k, v = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
-
-    def clear():
-        q.grad = k.grad = v.grad = None
-
+    t = Timings(fn, q, k, v, do)
     for _ in range(warmup):
-        clear()
-        fn(q, k, v).backward(do)
+        t.step()
     torch.cuda.synchronize()
-    fwd, bwd, both = [], [], []
-    for _ in range(reps):
-        with torch.no_grad():
-            fwd.append(event_ms(lambda: fn(q, k, v)))
-    for _ in range(reps):
-        clear()
-        o = fn(q, k, v)
-        torch.cuda.synchronize()
-        bwd.append(event_ms(lambda: o.backward(do)))
-        del o
-    for _ in range(reps):
-        clear()
-        both.append(event_ms(lambda: fn(q, k, v).backward(do)))
-    clear()
-    torch.cuda.synchronize()
-    torch.cuda.empty_cache()
-    base = torch.cuda.memory_allocated()
-    torch.cuda.reset_peak_memory_stats()
-    fn(q, k, v).backward(do)
-    torch.cuda.synchronize()
-    peak = (torch.cuda.max_memory_allocated() - base) / 2 ** 20
-    return statistics.median(fwd), statistics.median(bwd), statistics.median(both), peak
+    return t.forward_ms(reps), t.backward_ms(reps), t.step_ms(reps), t.peak_extra_mb()
 
 
-def fmt(x, spec):
-    return "" if x is None else format(x, spec)
+def _cell(value, spec):
+    return "" if value is None else format(value, spec)
+
+
+def _over(a, b):
+    return a / b if a and b else None
+
+
+# The three report tables: (heading, column names, cells of one (D, N) row given a lookup
+# get(impl, key) -> value or None).  Speedups are other_ms / fused_ms (>1 = fused faster).
+IMPLS3 = ("fused", "naive", "sdpa")
+TABLES = [
+    ("Forward + backward",
+     ["D", "N", "fused ms", "naive ms", "SDPA ms", "vs naive", "vs SDPA", "fused TFLOP/s", "SDPA TFLOP/s"],
+     lambda get: [_cell(get("fused", "fwd_bwd_ms"), ".3f"), _cell(get("naive", "fwd_bwd_ms"), ".3f") or "OOM",
+                  _cell(get("sdpa", "fwd_bwd_ms"), ".3f"),
+                  _cell(_over(get("naive", "fwd_bwd_ms"), get("fused", "fwd_bwd_ms")), ".2f"),
+                  _cell(_over(get("sdpa", "fwd_bwd_ms"), get("fused", "fwd_bwd_ms")), ".2f"),
+                  _cell(get("fused", "tflops"), ".1f"), _cell(get("sdpa", "tflops"), ".1f")]),
+    ("Backward only",
+     ["D", "N", "fused bwd ms", "naive bwd ms", "SDPA bwd ms", "vs naive", "vs SDPA", "fused bwd / fused fwd"],
+     lambda get: [_cell(get(i, "bwd_ms"), ".3f") for i in IMPLS3]
+                 + [_cell(_over(get("naive", "bwd_ms"), get("fused", "bwd_ms")), ".2f"),
+                    _cell(_over(get("sdpa", "bwd_ms"), get("fused", "bwd_ms")), ".2f"),
+                    _cell(_over(get("fused", "bwd_ms"), get("fused", "fwd_ms")), ".2f")]),
+    ("Peak extra memory (MB)",
+     ["D", "N", "fused", "naive", "SDPA", "naive / fused"],
+     lambda get: [_cell(get(i, "peak_mem_mb"), ".1f") for i in IMPLS3]
+                 + [_cell(_over(get("naive", "peak_mem_mb"), get("fused", "peak_mem_mb")), ".1f")]),
+]
 
 
 def markdown(rows, tile, gpu, B, H, reps):
-    ok = {(r["D"], r["N"], r["impl"]): r for r in rows if r["status"] == "ok"}
-    cfgs = sorted({(r["D"], r["N"]) for r in rows})
+    """The report in the reference's Markdown layout (same headings and columns)."""
+    done = {(r["D"], r["N"], r["impl"]): r for r in rows if r["status"] == "ok"}
+    configs = sorted({(r["D"], r["N"]) for r in rows})
+    out = [f"# Backward benchmark (fused tile {tile})", "",
+           f"GPU: {gpu}; B={B}, H={H}; FP16 inputs; causal. Median of {reps} runs.  ",
+           "Speedup = other_ms / fused_ms (>1 = fused faster). Memory = peak extra GPU memory during fwd+bwd."]
+    for heading, columns, cells in TABLES:
+        out += ["", f"## {heading}", "", "| " + " | ".join(columns) + " |", "|" + "---|" * len(columns)]
+        for D, N in configs:
+            def get(impl, key, D=D, N=N):
+                r = done.get((D, N, impl))
+                return None if r is None else r[key]
+            out.append("| " + " | ".join([str(D), str(N)] + cells(get)) + " |")
+    return "\n".join(out) + "\n"
 
-    def get(D, N, impl, key):
-        r = ok.get((D, N, impl))
-        return r[key] if r else None
 
-    def ratio(x, y):
-        return x / y if x and y else None
-
-    L = [f"# Backward benchmark (fused tile {tile})", "",
-         f"GPU: {gpu}; B={B}, H={H}; FP16 inputs; causal. Median of {reps} runs.  ",
-         "Speedup = other_ms / fused_ms (>1 = fused faster). Memory = peak extra GPU memory during fwd+bwd.", "",
-         "## Forward + backward", "",
-         "| D | N | fused ms | naive ms | SDPA ms | vs naive | vs SDPA | fused TFLOP/s | SDPA TFLOP/s |",
-         "|---|---|---|---|---|---|---|---|---|"]
-    for D, N in cfgs:
-        fu, na, sd = (get(D, N, i, "fwd_bwd_ms") for i in ("fused", "naive", "sdpa"))
-        L.append(f"| {D} | {N} | {fmt(fu, '.3f')} | {fmt(na, '.3f') or 'OOM'} | {fmt(sd, '.3f')} | "
-                 f"{fmt(ratio(na, fu), '.2f')} | {fmt(ratio(sd, fu), '.2f')} | "
-                 f"{fmt(get(D, N, 'fused', 'tflops'), '.1f')} | {fmt(get(D, N, 'sdpa', 'tflops'), '.1f')} |")
-    L += ["", "## Backward only", "",
-          "| D | N | fused bwd ms | naive bwd ms | SDPA bwd ms | vs naive | vs SDPA | fused bwd / fused fwd |",
-          "|---|---|---|---|---|---|---|---|"]
-    for D, N in cfgs:
-        fu, na, sd = (get(D, N, i, "bwd_ms") for i in ("fused", "naive", "sdpa"))
-        L.append(f"| {D} | {N} | {fmt(fu, '.3f')} | {fmt(na, '.3f')} | {fmt(sd, '.3f')} | "
-                 f"{fmt(ratio(na, fu), '.2f')} | {fmt(ratio(sd, fu), '.2f')} | "
-                 f"{fmt(ratio(fu, get(D, N, 'fused', 'fwd_ms')), '.2f')} |")
-    L += ["", "## Peak extra memory (MB)", "",
-          "| D | N | fused | naive | SDPA | naive / fused |", "|---|---|---|---|---|---|"]
-    for D, N in cfgs:
-        fu, na, sd = (get(D, N, i, "peak_mem_mb") for i in ("fused", "naive", "sdpa"))
-        L.append(f"| {D} | {N} | {fmt(fu, '.1f')} | {fmt(na, '.1f')} | {fmt(sd, '.1f')} | {fmt(ratio(na, fu), '.1f')} |")
-    return "\n".join(L) + "\n"
+def csv_row(r, B, H, tm, tn, gpu):
+    """One result dict as a CSV row: floats with four decimals, plus the run's constants."""
+    row = {key: (f"{val:.4f}" if isinstance(val, float) else val) for key, val in r.items()}
+    row.update(B=B, H=H, tile_m=tm, tile_n=tn, gpu=gpu)
+    return row
 
 
 def main():
@@ -175,9 +206,7 @@ def main():
     with open(csv_path, "w", newline="") as f:
         w = csv.DictWriter(f, fieldnames=fields)
         w.writeheader()
-        for r in rows:
-            w.writerow({**{k: (f"{v:.4f}" if isinstance(v, float) else v) for k, v in r.items()},
-                        "B": a.B, "H": a.H, "tile_m": tm, "tile_n": tn, "gpu": gpu})
+        w.writerows(csv_row(r, a.B, a.H, tm, tn, gpu) for r in rows)
     md_path = os.path.join(a.out_dir, f"bench_backward_{tile}.md")
     with open(md_path, "w") as f:
         f.write(markdown(rows, tile, gpu, a.B, a.H, a.reps))

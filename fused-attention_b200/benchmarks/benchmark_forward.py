@@ -13,6 +13,9 @@ CSV columns, so B200 rows line up with the reference's `results/benchmarks/fused
 Run from the repository root:
     python fused-attention_b200/benchmarks/benchmark_forward.py --tile-m 64 --tile-n 128
 Outputs: results/benchmarks/fused/<tag>/<tile>/bench_forward_{sep,agg}_<tag>_<tile>.csv
+The per-configuration CSV has the reference's columns plus `kernel_tiles`, the tile shape the
+sm_100a kernel ran (`q128_kv64` or `q128_kv128`; empty for other implementations): the kernel's
+query tile is always 128 rows, so tile_m is not a kernel parameter here.
 """
 import argparse
 import csv
@@ -26,7 +29,20 @@ import torch
 import torch.nn.functional as F
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
 DEFAULT_KERNEL = os.path.join(os.path.dirname(HERE), "attention", "fused", "fused.py")
+
+
+def kernel_label(path):
+    """The kernel file as written into the CSVs: relative to the repository root when inside it."""
+    full = os.path.abspath(path)
+    return os.path.relpath(full, REPO) if full.startswith(REPO + os.sep) else os.path.basename(full)
+
+
+def kernel_tiles(tile_n):
+    """Tile shape the sm_100a forward runs for the reference's (tile_m, tile_n) knobs: 128 query
+    rows always (tile_m only takes part in the divisibility rule), 64 or 128 keys per K/V tile."""
+    return f"q128_kv{64 if tile_n <= 64 else 128}"
 
 
 def load_kernel(path, name="fused_attention"):
@@ -151,13 +167,14 @@ def main():
             del q, k, v
             torch.cuda.empty_cache()
     speedups(rows)
+    label = kernel_label(a.kernel)
     for r in rows:
-        r += [gpu, a.kernel]
+        r += [gpu, label, kernel_tiles(a.tile_n) if r[4] == "fused" and a.kernel == DEFAULT_KERNEL else ""]
     os.makedirs(os.path.dirname(out) or ".", exist_ok=True)
     with open(out, "w", newline="") as f:
         w = csv.writer(f)
         w.writerow(["D", "N", "B", "H", "impl", "tile_m", "tile_n", "median_ms", "tflops", "first_call_ms",
-                    "fused_speedup_vs_unfused", "fused_speedup_vs_sdpa", "gpu", "kernel"])
+                    "fused_speedup_vs_unfused", "fused_speedup_vs_sdpa", "gpu", "kernel", "kernel_tiles"])
         w.writerows(rows)
     header, body = summary_rows(rows)
     os.makedirs(os.path.dirname(summary_out) or ".", exist_ok=True)

@@ -42,7 +42,7 @@ def _forward_bench():
 
 
 SEP_COLUMNS = ["D", "N", "B", "H", "impl", "tile_m", "tile_n", "median_ms", "tflops", "first_call_ms",
-               "H_kv", "fused_speedup_vs_unfused", "fused_speedup_vs_sdpa", "gpu", "kernel"]
+               "H_kv", "fused_speedup_vs_unfused", "fused_speedup_vs_sdpa", "gpu", "kernel", "kernel_tiles"]
 
 
 def output_paths(tag, tile_m, tile_n, h_kv):
@@ -107,7 +107,8 @@ def main(argv=None):
             torch.cuda.empty_cache()
     fb.speedups(rows)
     for r in rows:
-        r += [gpu, a.kernel]
+        r += [gpu, fb.kernel_label(a.kernel),
+              fb.kernel_tiles(a.tile_n) if r[4] == "fused" and a.kernel == DEFAULT_KERNEL else ""]
     os.makedirs(os.path.dirname(out) or ".", exist_ok=True)
     with open(out, "w", newline="") as f:
         w = csv.writer(f)

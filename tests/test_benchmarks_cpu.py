@@ -50,7 +50,7 @@ def test_gqa_rows_keep_the_reference_columns():
     rows = _rows(h_kv=2)
     fb.speedups(rows)
     for r in rows:
-        r += ["NVIDIA B200", "kernel.py"]
+        r += ["NVIDIA B200", "kernel.py", fb.kernel_tiles(64) if r[4] == "fused" else ""]
         assert len(r) == len(gq.SEP_COLUMNS)
         assert r[gq.SEP_COLUMNS.index("H_kv")] == 2
     header, body = fb.summary_rows(rows)
@@ -64,3 +64,11 @@ def test_gqa_cli_rejects_a_head_count_that_does_not_divide():
     gq = _load("benchmark_forward_gqa")
     with pytest.raises(SystemExit):
         gq.main(["--H", "8", "--H-kv", "3"])
+
+
+def test_csv_kernel_columns_name_no_machine_path():
+    """The kernel column is repository-relative and kernel_tiles names the tile shape that ran."""
+    fb = _load("benchmark_forward")
+    assert fb.kernel_label(fb.DEFAULT_KERNEL) == "fused-attention_b200/attention/fused/fused.py"
+    assert fb.kernel_label("/elsewhere/custom_kernel.py") == "custom_kernel.py"
+    assert [fb.kernel_tiles(n) for n in (32, 64, 128, 256)] == ["q128_kv64", "q128_kv64", "q128_kv128", "q128_kv128"]

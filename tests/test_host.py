@@ -110,9 +110,9 @@ def test_backward_rejects_unsupported_head_dims_before_touching_the_device():
         assert lib.fa_bwd_noalloc(p, p, p, p, p, p, p, p, p, 1, 8, 8, 128, D, 0, 64, 64, p, None) == 2
 
 
-def test_wrappers_launch_the_128_key_tile(monkeypatch):
+def test_wrappers_launch_the_requested_kv_tile(monkeypatch):
     """The drop-in wrappers check the caller's tile_m / tile_n against N (the reference's rule) and
-    then launch the forward kernel with its 128-key K/V tile, whatever tile_n was."""
+    launch the forward kernel with the K/V tile tile_n selects: 64 keys for tile_n <= 64, else 128."""
     from attention.fused.fused import fused_attention
     from attention.gqa.fused_gqa import fused_gqa_attention
     from attention.backward.fused_backward import _forward
@@ -123,10 +123,14 @@ def test_wrappers_launch_the_128_key_tile(monkeypatch):
     kv = torch.zeros(1, 2, 128, 64, dtype=torch.float16)
     fused_attention(q, q, q)
     fused_attention(q, q, q, 128, 64)
+    fused_attention(q, q, q, 64, 128)
     fused_gqa_attention(q, kv, kv, 64, 64)
+    fused_gqa_attention(q, kv, kv, 64, 128)
     _forward(q, q, q, 64, 64)
-    assert calls == [(64, 128, True), (128, 128, True), (64, 128, True), (64, 128, False)]
-    assert nat.FWD_KV_TILE == 128
+    _forward(q, q, q, 64, 128)
+    assert calls == [(64, 64, True), (128, 64, True), (64, 128, True), (64, 64, True), (64, 128, True),
+                     (64, 64, False), (64, 128, False)]
+    assert [nat.kv_tile(t) for t in (16, 32, 64, 128, 256)] == [64, 64, 64, 128, 128]
 
 
 def test_python_wrappers_keep_reference_errors():
