@@ -4,18 +4,22 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...           (N > 1, one rank per GPU)
 
-Workload (BASELINE config 2 at the metric's point): causal MHA, B=4, H=32, S=8192, D=128, fp16,
-Q/K/V/dO i.i.d. N(0,1) (synthetic, seeded).  One step = forward + backward through the public
-autograd API (fused_attention_autograd: LSE-saving forward, delta, dK/dV, dQ kernels).  With N
-GPUs every rank owns the same per-GPU work (weak scaling: global batch 4N) through
+Workload (default, BASELINE config 2 at the metric's point): causal MHA, B=4, H=32, S=8192,
+D=128, fp16, Q/K/V/dO i.i.d. N(0,1) (synthetic, seeded).  One step = forward + backward through
+the public autograd API (fused_attention_autograd: LSE-saving forward, delta, dK/dV, dQ kernels).
+With N GPUs every rank owns the same per-GPU work (weak scaling: global batch 4N) through
 attention.dist.sharded_attention_autograd, which all-gathers O and dQ/dK/dV over NCCL.
+--workload c5: BASELINE config 5, causal GQA fwd+bwd, B=8, H=32, H_kv=8, D=128, bf16, S=32768
+(--seq 8192 / 16384 for the other points), the same global job on every N (strong scaling).
 
 value  = fwd+bwd causal TFLOP/s of the whole job (3.5 * 2 * B * H * S^2 * D per step, the
          reference's convention), device time, max over ranks, inputs resident in HBM.
 e2e    = the same metric with pinned-host inputs copied in and O/dQ/dK/dV copied out every step
          (batch slices pipelined: copy-in, compute and copy-out of different slices overlap).
-roofline: the dominant kernel, timed alone with CUDA events on its launch stream.
-cpu_baseline: the reference's PyTorch fp32 path on the host cores, on a bounded sample.
+roofline: the dominant kernel, timed alone with CUDA events on its launch stream, in rounds
+         interleaved with untimed steps (so the kernels run in the step loop's clock state).
+cpu_baseline: the reference's PyTorch fp32 path on the host cores, on a bounded sample (plus
+         torch's causal SDPA on the same sample).
 --impl reference: the reference's CPU implementation (oracle port) timed the same way.
 """
 import argparse
@@ -45,17 +49,30 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--batch", type=int, default=4, help="per-GPU batch")
+    ap.add_argument("--workload", choices=["c2", "c5"], default="c2",
+                    help="c2: B=4/GPU H=32 S=8192 D=128 fp16 MHA, weak scaling (the metric's point); "
+                         "c5: B=8 H=32 H_kv=8 D=128 bf16 S=32768, strong scaling")
+    ap.add_argument("--batch", type=int, default=None, help="per-GPU batch (c2) / global batch (c5)")
     ap.add_argument("--heads", type=int, default=32)
-    ap.add_argument("--kv-heads", type=int, default=0, help="0 = MHA")
-    ap.add_argument("--seq", type=int, default=8192)
+    ap.add_argument("--kv-heads", type=int, default=None, help="0 = MHA")
+    ap.add_argument("--seq", type=int, default=None)
     ap.add_argument("--dim", type=int, default=128)
-    ap.add_argument("--dtype", choices=["fp16", "bf16"], default="fp16")
+    ap.add_argument("--dtype", choices=["fp16", "bf16"], default=None)
     ap.add_argument("--tile-m", type=int, default=64)
     ap.add_argument("--tile-n", type=int, default=128)
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=None, help="default: --steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    return ap.parse_args()
+    a = ap.parse_args()
+    c5 = a.workload == "c5"
+    defaults = {"batch": 8 if c5 else 4, "kv_heads": 8 if c5 else 0, "seq": 32768 if c5 else 8192,
+                "dtype": "bf16" if c5 else "fp16"}
+    for key, val in defaults.items():
+        if getattr(a, key) is None:
+            setattr(a, key, val)
+    a.strong = c5
+    if a.e2e_steps is None:
+        a.e2e_steps = a.steps
+    return a
 
 
 def load_peaks():
@@ -143,12 +160,24 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# Longest sequence the CPU sample runs: the explicit path keeps S x S fp32 matrices for autograd
+# (4 GiB each at S=32768), so longer configurations are sampled at this length.
+CPU_SAMPLE_MAX_S = 8192
+
+
 def cpu_baseline_sample(S, D, reps=3):
-    from oracle.cpu_baseline import time_fwd_bwd
-    secs, flops, threads = time_fwd_bwd(S, D, heads=1, reps=reps)
+    from oracle.cpu_baseline import time_fwd_bwd, time_sdpa_fwd_bwd
+    Ss = min(S, CPU_SAMPLE_MAX_S)
+    secs, flops, threads = time_fwd_bwd(Ss, D, heads=1, reps=reps)
+    time_sdpa_fwd_bwd(min(Ss, 1024), D, heads=1, reps=1)  # first call: one-time set-up, untimed
+    s_secs, s_flops, _ = time_sdpa_fwd_bwd(Ss, D, heads=1, reps=reps)
+    note = "" if Ss == S else f" (the workload's S={S} sampled at S={Ss})"
     return {"value": flops / secs / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"1 (batch, head) pair of the workload (S={S}, D={D}), fp32 fwd+bwd through "
-                      f"torch autograd of the explicit reference path, median of {reps}"}
+            "sample": f"1 (batch, head) pair of the workload (S={Ss}, D={D}){note}, fp32 fwd+bwd through "
+                      f"torch autograd of the explicit reference path, median of {reps}",
+            "sdpa": {"value": s_flops / s_secs / 1e12, "unit": UNIT, "cores": threads,
+                     "sample": f"the same (batch, head) pair through torch.nn.functional."
+                               f"scaled_dot_product_attention(is_causal=True), fp32 fwd+bwd, median of {reps}"}}
 
 
 def run_reference_arm(a, rank):
@@ -156,7 +185,7 @@ def run_reference_arm(a, rank):
     if rank != 0:
         return
     from oracle.cpu_baseline import time_fwd_bwd
-    S, D = a.seq, a.dim
+    S, D = min(a.seq, CPU_SAMPLE_MAX_S), a.dim
     for _ in range(a.warmup):
         time_fwd_bwd(S, D, heads=1, reps=1)
     times = []
@@ -167,11 +196,13 @@ def run_reference_arm(a, rank):
         times.append(t)
     total = sum(times)
     value = flops * a.steps / total / 1e12
-    sample = (f"per step: 1 (batch, head) pair of B={a.batch} H={a.heads} S={S} D={D}, fp32 fwd+bwd via "
-              f"torch autograd of the reference's explicit path on the CPU")
+    sample = (f"per step: 1 (batch, head) pair of B={a.batch} H={a.heads} S={a.seq} D={D}"
+              + ("" if S == a.seq else f" sampled at S={S}")
+              + ", fp32 fwd+bwd via torch autograd of the reference's explicit path on the CPU")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": a.gpus,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1000 * total / a.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "strong" if a.strong else "weak", "vs_baseline": None,
+            "dtype": "f32",
             "data": "synthetic", "config": workload_config(a, 1),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -179,11 +210,19 @@ def run_reference_arm(a, rank):
 
 
 def workload_config(a, world):
-    return {"workload": f"causal {'GQA' if a.kv_heads and a.kv_heads != a.heads else 'MHA'} fwd+bwd, "
-                        f"B={a.batch}/GPU H={a.heads} H_kv={a.kv_heads or a.heads} S={a.seq} D={a.dim} {a.dtype}",
-            "global_batch": a.batch * world, "per_gpu_batch": a.batch, "heads": a.heads,
+    kind = "GQA" if a.kv_heads and a.kv_heads != a.heads else "MHA"
+    if a.strong:
+        name = (f"BASELINE config 5: causal {kind} fwd+bwd, B={a.batch} (global) H={a.heads} "
+                f"H_kv={a.kv_heads or a.heads} S={a.seq} D={a.dim} {a.dtype}")
+        global_b, per_gpu = a.batch, a.batch / world
+    else:
+        name = (f"causal {kind} fwd+bwd, B={a.batch}/GPU H={a.heads} H_kv={a.kv_heads or a.heads} "
+                f"S={a.seq} D={a.dim} {a.dtype}")
+        global_b, per_gpu = a.batch * world, a.batch
+    return {"workload": name, "global_batch": global_b, "per_gpu_batch": per_gpu, "heads": a.heads,
             "kv_heads": a.kv_heads or a.heads, "seq_len": a.seq, "head_dim": a.dim,
-            "tiles": f"{a.tile_m}x{a.tile_n}", "parallelism": f"batch x head shards over {world} GPU(s)",
+            "tiles": f"{a.tile_m}x{a.tile_n} (kernel: 128-row query tiles, {64 if a.tile_n <= 64 else 128}-key K/V tiles)",
+            "parallelism": f"(batch, K/V head) shards over {world} GPU(s)",
             "l2": "inputs larger than L2 (4 x B*H*S*D*2 bytes per step vs 126 MB)"}
 
 
@@ -215,7 +254,7 @@ def main():
     from attention.dist import sharded_attention_autograd
 
     dt = torch.float16 if a.dtype == "fp16" else torch.bfloat16
-    B = a.batch * world
+    B = a.batch if a.strong else a.batch * world
     H, S, D = a.heads, a.seq, a.dim
     H_kv = a.kv_heads or H
     g = torch.Generator(device=dev).manual_seed(1234)
@@ -299,11 +338,16 @@ def main():
         "bwd_dkdv": (lambda: nat.bwd_dkdv(qs, ks, vs, dos, lse_s, delta, dk_s, dv_s, a.tile_m, a.tile_n), 4.0),
         "bwd_dq": (lambda: nat.bwd_dq(qs, ks, vs, dos, lse_s, delta, dq_s, a.tile_m, a.tile_n), 3.0),
     }
-    kt = {}
-    reps = max(3, min(10, a.steps))
-    for name, (fn, _) in kern.items():
+    # Each round runs one untimed step (which keeps the GPU in the step loop's clock and power
+    # state) and then times every kernel once; a kernel's time is its median over the rounds.
+    for fn, _ in kern.values():
         fn()
-        kt[name] = timed(fn, reps) / reps
+    samples = {name: [] for name in kern}
+    for _ in range(max(3, min(10, a.steps))):
+        step()
+        for name, (fn, _) in kern.items():
+            samples[name].append(timed(fn, 1))
+    kt = {name: statistics.median(v) for name, v in samples.items()}
     nat.check_status(dev)
     shard_unit_flops = units * grp * S * S * D  # one causal S x S x D GEMM over the shard
     dominant = max(kt, key=kt.get)
@@ -394,7 +438,8 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
                 "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f16" if a.dtype == "fp16" else "bf16",
+                "scaling": "strong" if a.strong else "weak", "vs_baseline": None,
+                "dtype": "f16" if a.dtype == "fp16" else "bf16",
                 "data": "synthetic (i.i.d. N(0,1), seeded)", "config": workload_config(a, world),
                 "fwd_tflops": fwd_tflops, "fwd_ms_per_step": ms_fwd / a.steps,
                 "frac_of_spec_peak": {"fwd+bwd": value / (SPEC_PEAK * world), "fwd": fwd_tflops / (SPEC_PEAK * world)},

@@ -6,6 +6,12 @@
 
 The shared library lands next to the Python package (attention/libfa_sm100.so), so it travels
 with the source tree.  Objects go to _build/ (not committed).
+
+build_stall_test() compiles the same sources into _build/libfa_sm100_stalltest.so for the
+failure-detection GPU test only: every kernel's UMMA issuer waits at pipeline step 1 on an
+mbarrier that nothing arrives at, with a 20 ms pipeline-wait limit (teardown waits keep their 2 s
+limit), so the kernels' bounded-wait abort path runs on a normal input.  The product library
+never contains that wait.
 """
 import argparse
 import os
@@ -17,6 +23,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 OUT = os.path.join(HERE, "attention", "libfa_sm100.so")
+STALL_OUT = os.path.join(BUILD, "libfa_sm100_stalltest.so")
+STALL_FLAGS = ["-DFA_TEST_STALL_STEP=1", "-DFA_WAIT_TIMEOUT_NS=20000000ull"]
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 SOURCES = ["fa_api.cu", "fa_fwd.cu", "fa_bwd.cu", "fa_noalloc.cu"]
 HEADERS = ["fa_sm100.cuh", "fa_internal.h"]
@@ -34,17 +42,17 @@ def _newer(src_list, target):
     return any(os.path.getmtime(s) > t for s in src_list)
 
 
-def build(force=False, verbose=False):
-    os.makedirs(BUILD, exist_ok=True)
+def build(force=False, verbose=False, out=OUT, extra_flags=(), obj_dir=BUILD):
+    os.makedirs(obj_dir, exist_ok=True)
     headers = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(INCLUDE, "fa_sm100.h")]
     jobs = []
     objs = []
     for src in SOURCES:
         s = os.path.join(CSRC, src)
-        o = os.path.join(BUILD, src.replace(".cu", ".o"))
+        o = os.path.join(obj_dir, src.replace(".cu", ".o"))
         objs.append(o)
         if force or _newer([s] + headers, o):
-            cmd = [NVCC, *ARCH, *FLAGS, "-c", s, "-o", o]
+            cmd = [NVCC, *ARCH, *FLAGS, *extra_flags, "-c", s, "-o", o]
             if verbose:
                 cmd += ["-Xptxas", "-v"]
             jobs.append((src, cmd))
@@ -62,13 +70,19 @@ def build(force=False, verbose=False):
             failed |= r.returncode != 0
     if failed:
         raise RuntimeError("nvcc failed")
-    if force or jobs or _newer(objs, OUT):
-        cmd = [NVCC, *ARCH, "-shared", "-Xcompiler", "-fPIC", "-o", OUT, *objs, "-lcudart_static"]
+    if force or jobs or _newer(objs, out):
+        cmd = [NVCC, *ARCH, "-shared", "-Xcompiler", "-fPIC", "-o", out, *objs, "-lcudart_static"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             sys.stderr.write(r.stdout + r.stderr)
             raise RuntimeError("link failed")
-    return OUT
+    return out
+
+
+def build_stall_test(force=False, verbose=False):
+    """The failure-detection test library (see the module docstring)."""
+    return build(force, verbose, out=STALL_OUT, extra_flags=STALL_FLAGS,
+                 obj_dir=os.path.join(BUILD, "stalltest"))
 
 
 if __name__ == "__main__":
@@ -77,3 +91,4 @@ if __name__ == "__main__":
     ap.add_argument("--verbose", action="store_true")
     a = ap.parse_args()
     print(build(force=a.force, verbose=a.verbose))
+    print(build_stall_test(force=a.force))

@@ -251,7 +251,8 @@ struct DqCfg {
 
 enum : int {
   DQ_OUTER = 0, DQ_KFULL = 1, DQ_KEMPTY = 5, DQ_VFULL = 9, DQ_VEMPTY = 13, DQ_SFULL = 17, DQ_SFREE = 18,
-  DQ_DPFULL = 19 /* + 2 */, DQ_DSREADY = 21 /* + 2 */, DQ_ACC = 23, DQ_DRAIN = 24
+  DQ_DPFULL = 19 /* + 2 */, DQ_DSREADY = 21 /* + 2 */, DQ_ACC = 23, DQ_DRAIN = 24,
+  DQ_NEVER = 25 /* never arrived at (failure-detection test build) */
 };
 
 template <int D, bool BF16>
@@ -288,6 +289,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(BAR(DQ_DSREADY + 1), 256);
     mbar_init(BAR(DQ_ACC), 1);
     mbar_init(BAR(DQ_DRAIN), 1);
+    mbar_init(BAR(DQ_NEVER), 1);
     fence_barrier_init();
   }
   uint32_t tmem;
@@ -361,6 +363,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           umma_commit_w(BAR(DQ_VEMPTY + 0));
         }
         for (int s = 0; ok && s < nsteps; ++s) {
+          FA_STALL_HERE(s, BAR(DQ_NEVER), p.status, ok)
           if (s + 1 < nsteps) {
             const int k1 = (s + 1) % KST, v1 = (s + 1) % VST;
             if (!(ok = warp_all(mbar_wait(BAR(DQ_SFREE), s & 1, p.status, kDevTimeoutBwd)))) break;
@@ -496,7 +499,8 @@ struct DkdvCfg {
 enum : int {
   KV_OUTER = 0, KV_QFULL = 1 /* + Q stage (4) */, KV_QEMPTY = 5 /* + Q stage (4) */,
   KV_OFULL = 9 /* + dO stage (2) */, KV_OEMPTY = 11 /* + dO stage (2) */, KV_STFULL = 13,
-  KV_PREADY = 14, KV_DPFULL = 15, KV_DSREADY = 16, KV_ACC = 17, KV_DRAIN = 18
+  KV_PREADY = 14, KV_DPFULL = 15, KV_DSREADY = 16, KV_ACC = 17, KV_DRAIN = 18,
+  KV_NEVER = 19 /* never arrived at (failure-detection test build) */
 };
 
 template <int D, bool BF16>
@@ -533,6 +537,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(BAR(KV_DSREADY), 256);
     mbar_init(BAR(KV_ACC), 1);
     mbar_init(BAR(KV_DRAIN), 1);
+    mbar_init(BAR(KV_NEVER), 1);
     fence_barrier_init();
   }
   uint32_t tmem;
@@ -620,6 +625,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         for (int s = 0; ok && s < nsteps; ++s) {
           const int qs = s % QST, os = s % OST;
+          FA_STALL_HERE(s, BAR(KV_NEVER), p.status, ok)
           if (!(ok = warp_all(mbar_wait(BAR(KV_PREADY), s & 1, p.status, kDevTimeoutBwd)))) break;
           tc_fence_after();
           umma_tmem_tile<D, BF16>(tDV, tST, desc_add(dOm, os * C::kTile), s > 0 ? 1u : 0u);  // dV += P^T dO

@@ -91,7 +91,8 @@ enum : int {
   BAR_OFULL = 21,   // + tile (2)
   BAR_DRAIN = 23,
   BAR_PFULLB = 24,  // + tile (2): P of the second half
-  BAR_COUNT = 26
+  BAR_NEVER = 26,   // never arrived at (the failure-detection test build waits on it)
+  BAR_COUNT = 27
 };
 
 struct QTile {
@@ -297,6 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(BAR(BAR_OFULL + t), 1);
     }
     mbar_init(BAR(BAR_DRAIN), 1);
+    mbar_init(BAR(BAR_NEVER), 1);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -380,6 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ks1 = (j + 1) % KST;
         const uint64_t dvj = dv0 + static_cast<uint64_t>((vs * C::kKVBytes) >> 4);
         const uint64_t dkn = dk0 + static_cast<uint64_t>((ks1 * C::kKVBytes) >> 4);
+        FA_STALL_HERE(j, BAR(BAR_NEVER), p.status, ok)
         if (!(ok = warp_all(mbar_wait(BAR(BAR_VFULL + vs), (j / VST) & 1, p.status, kDevTimeoutKV)))) break;
         bool k_ready = false;
         bool issued_s = false;

@@ -19,6 +19,23 @@
 #ifndef FA_WAIT_TIMEOUT_NS
 #define FA_WAIT_TIMEOUT_NS 2000000000ull  // 2 s: far above any legitimate pipeline wait
 #endif
+// Limit of the teardown waits for a CTA's own copies and UMMAs in flight (they always complete;
+// this stays long even in the failure-detection test build, whose pipeline limit is short).
+#ifndef FA_DRAIN_TIMEOUT_NS
+#define FA_DRAIN_TIMEOUT_NS 2000000000ull
+#endif
+
+// Failure-detection test build only (the library built with -DFA_TEST_STALL_STEP=n, never the
+// product library): at pipeline step n the UMMA issuer of every kernel waits on an mbarrier that
+// nothing arrives at, so its bounded wait runs out and the kernel's abort path runs.
+#ifdef FA_TEST_STALL_STEP
+#define FA_STALL_HERE(step, bar, status, ok)                                              \
+  if ((step) == FA_TEST_STALL_STEP) {                                                    \
+    if (!((ok) = warp_all(mbar_wait((bar), 0, (status), kDevTestStall)))) break;         \
+  }
+#else
+#define FA_STALL_HERE(step, bar, status, ok)
+#endif
 
 namespace fa {
 
@@ -36,6 +53,7 @@ enum DeviceError : int {
   kDevTimeoutDrain = 107,   // teardown waiting for in-flight copies / MMAs
   kDevTimeoutBwd = 108,     // backward pipeline wait
   kDevSmemLayout = 109,     // dynamic shared memory start leaves too little alignment slack
+  kDevTestStall = 110,      // failure-detection test build: the injected wait ran out
   kDevAborted = 199,        // another CTA already failed; this one stopped early
 };
 
@@ -126,32 +144,11 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int* s
   if (mbar_try_wait(bar, parity)) return;
   const uint64_t t0 = global_timer_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (global_timer_ns() - t0 > FA_WAIT_TIMEOUT_NS) {
+    if (global_timer_ns() - t0 > FA_DRAIN_TIMEOUT_NS) {
       record_error(status, kDevTimeoutDrain, static_cast<int>(threadIdx.x));
       return;
     }
   }
-}
-
-// ---------------------------------------------------------------- named barriers
-__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-
-// Named barrier that also ANDs a flag over the participating threads.  Used where a group of
-// warps must leave a pipelined loop together when any of them saw a failed (timed-out) wait,
-// so that no thread is ever left waiting at a barrier its partners skipped.
-__device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t nthreads, bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred ps, pd;\n\t"
-      "setp.ne.u32 ps, %3, 0;\n\t"
-      "bar.red.and.pred pd, %1, %2, ps;\n\t"
-      "selp.u32 %0, 1, 0, pd;\n\t}\n"
-      : "=r"(r)
-      : "r"(id), "r"(nthreads), "r"(static_cast<uint32_t>(v))
-      : "memory");
-  return r != 0;
 }
 
 // Warp-uniform result of a bounded wait: lanes of a warp must agree before warp-collective
