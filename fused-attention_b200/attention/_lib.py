@@ -47,6 +47,7 @@ SIGNATURES = {
     "fa_bwd_dkdv": [_VP, _VP, _VP, _VP, _FP, _FP, _VP, _VP, _I, _I, _I, _I, _I, _I, _I, _I, _VP, _VP],
     "fa_bwd_dq": [_VP, _VP, _VP, _VP, _FP, _FP, _VP, _I, _I, _I, _I, _I, _I, _I, _I, _VP, _VP],
     "fa_bwd_noalloc": [_VP, _VP, _VP, _VP, _VP, _FP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I, _I, _I, _VP, _VP],
+    "fa_unfused_fwd": [_VP, _VP, _VP, _VP, _FP, _VP, _I, _I, _I, _I, _I, _I, _VP, _VP],
 }
 _RESTYPES = {"fa_strerror": ctypes.c_char_p, "fa_last_cuda_error": ctypes.c_char_p}
 
@@ -180,6 +181,19 @@ def bwd_dq(q, k, v, do, lse, delta, dq, tile_m, tile_n):
                            _ptr(status_tensor(q.device)), _stream(q))
     if rc != FA_OK:
         _raise(rc, "fa_bwd_dq")
+
+
+def unfused_fwd(q, k, v, o, s, p):
+    """Enqueue the unfused three-kernel forward: s (fp32 [B, H, N, N]) = masked scaled scores,
+    p (dtype of q, [B, H, N, N]) = row softmax, o = p v."""
+    lib = load()
+    B, H, S, D = q.shape
+    H_kv = k.shape[1]
+    with torch.cuda.device(q.device):
+        rc = lib.fa_unfused_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(s), _ptr(p), B, H, H_kv, S, D,
+                                _dtype_code(q), _ptr(status_tensor(q.device)), _stream(q))
+    if rc != FA_OK:
+        _raise(rc, "fa_unfused_fwd")
 
 
 def load_by_path():

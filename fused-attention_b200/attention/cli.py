@@ -5,8 +5,8 @@ Behaviour follows the reference's `run_attention.py:33-130` / `run_attention_gqa
 usage error, 1 runtime failure; non-finite or wrongly shaped output is a runtime failure.
 
 Backends: `cutile` (the reference's name for its fused kernel; here the sm_100a kernel),
-`fused` (alias of `cutile`), `unfused` (the reference's 3-kernel cuTile baseline: not built on
-B200, reported as not implemented, exit 1), `reference` (PyTorch fp32).
+`fused` (alias of `cutile`), `unfused` (the reference's three-kernel baseline, as sm_100a
+kernels), `reference` (PyTorch fp32).
 """
 import argparse
 import sys

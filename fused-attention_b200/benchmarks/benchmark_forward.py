@@ -7,8 +7,8 @@ CSV columns, so B200 rows line up with the reference's `results/benchmarks/fused
 
   fused    attention.fused.fused.fused_attention (sm_100a kernel; or any kernel file via --kernel)
   sdpa     torch.nn.functional.scaled_dot_product_attention(is_causal=True)
-  unfused  the reference's 3-kernel cuTile baseline is not built for B200: its rows carry empty
-           timings, exactly as the reference writes a configuration that failed.
+  unfused  attention.fused.unfused.unfused_attention, the reference's three-kernel baseline (S and
+           P materialised in global memory) as sm_100a kernels
 
 Run from the repository root:
     python fused-attention_b200/benchmarks/benchmark_forward.py --tile-m 64 --tile-n 128
@@ -54,12 +54,20 @@ def load_kernel(path, name="fused_attention"):
     return getattr(mod, name)
 
 
-class NotBuilt(RuntimeError):
-    pass
+UNFUSED = os.path.join(os.path.dirname(HERE), "attention", "fused", "unfused.py")
+
+
+UNFUSED_GQA = os.path.join(os.path.dirname(HERE), "attention", "gqa", "unfused_gqa.py")
+_loaded = {}
 
 
 def unfused_attention(q, k, v, tm, tn):
-    raise NotBuilt("the reference's unfused cuTile baseline is not built for B200")
+    """The unfused baseline: unfused_attention for MHA, unfused_gqa_attention when K/V have fewer
+    heads (both run the same three kernels)."""
+    key = (UNFUSED, "unfused_attention") if k.shape == q.shape else (UNFUSED_GQA, "unfused_gqa_attention")
+    if key not in _loaded:
+        _loaded[key] = load_kernel(*key)
+    return _loaded[key](q, k, v, tm, tn)
 
 
 def time_call(fn, warmup=10, reps=30):

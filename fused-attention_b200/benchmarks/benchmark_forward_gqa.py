@@ -9,8 +9,8 @@ line up with the reference's `results/benchmarks/fused_gqa/...` files.  FLOPs ar
 
   fused    attention.gqa.fused_gqa.fused_gqa_attention (sm_100a kernel; or any kernel file via --kernel)
   sdpa     torch.nn.functional.scaled_dot_product_attention(is_causal=True, enable_gqa=True)
-  unfused  the reference's cuTile GQA baseline is not built for B200: its rows carry empty timings,
-           exactly as the reference writes a configuration that failed.
+  unfused  attention.gqa.unfused_gqa.unfused_gqa_attention, the reference's three-kernel GQA
+           baseline (S and P materialised in global memory) as sm_100a kernels
 
 --dtype bf16 and --Ds/--Ns/--B/--H cover BASELINE config 3 (B=4 H=32 S=8192 D=128 bf16):
     python fused-attention_b200/benchmarks/benchmark_forward_gqa.py --B 4 --H 32 --H-kv 2 \\

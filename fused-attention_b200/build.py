@@ -26,7 +26,7 @@ OUT = os.path.join(HERE, "attention", "libfa_sm100.so")
 STALL_OUT = os.path.join(BUILD, "libfa_sm100_stalltest.so")
 STALL_FLAGS = ["-DFA_TEST_STALL_STEP=1", "-DFA_WAIT_TIMEOUT_NS=20000000ull"]
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
-SOURCES = ["fa_api.cu", "fa_fwd.cu", "fa_bwd.cu", "fa_noalloc.cu"]
+SOURCES = ["fa_api.cu", "fa_fwd.cu", "fa_bwd.cu", "fa_noalloc.cu", "fa_unfused.cu"]
 HEADERS = ["fa_sm100.cuh", "fa_internal.h"]
 
 NVCC = os.environ.get("NVCC", "nvcc")

@@ -263,4 +263,37 @@ int fa_bwd_dq(const void* q, const void* k, const void* v, const void* dO, const
   return e == cudaSuccess ? FA_OK : cuda_fail(e);
 }
 
+int fa_unfused_fwd(const void* q, const void* k, const void* v, void* o, float* s_buf, void* p_buf,
+                   int B, int H, int H_kv, int S, int D, int dtype, int* dev_status, void* stream) {
+  if (!q || !k || !v || !o || !s_buf || !p_buf) return FA_ERR_INVALID_ARG;
+  int rc = check_common(B, H, H_kv, S, D, dtype, 128, 128, dev_status);
+  if (rc != FA_OK) return rc;
+  // P rows must be 16-byte aligned for its tensor map; grid.y holds B * H.
+  if (S % 8 != 0 || static_cast<long long>(B) * H > 65535) return FA_ERR_UNSUPPORTED;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(s_buf) ||
+      !aligned16(p_buf))
+    return FA_ERR_ALIGNMENT;
+  if ((rc = check_device()) != FA_OK) return rc;
+  CUtensorMap tmQ, tmK, tmP, tmV;
+  if ((rc = make_map(&tmQ, q, B * H, S, D, dtype, 128)) != FA_OK) return rc;
+  if ((rc = make_map(&tmK, k, B * H_kv, S, D, dtype, 128)) != FA_OK) return rc;
+  if ((rc = make_map(&tmV, v, B * H_kv, S, D, dtype, 128)) != FA_OK) return rc;
+  // P viewed as [B * H, S rows, S columns]: 64-column boxes of 128 rows (the score tiles' rows).
+  if ((rc = make_map(&tmP, p_buf, B * H, S, S, dtype, 128)) != FA_OK) return rc;
+  fa::UnfParams p{};
+  p.o = o;
+  p.s = s_buf;
+  p.p = p_buf;
+  p.status = dev_status;
+  p.N = S;
+  p.H = H;
+  p.H_kv = H_kv;
+  p.group = H / H_kv;
+  p.B = B;
+  p.sm_scale = 1.0f / sqrtf(static_cast<float>(D));
+  cudaError_t e = fa::launch_unfused(tmQ, tmK, tmP, tmV, p, D, dtype == FA_DTYPE_BF16,
+                                     static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? FA_OK : cuda_fail(e);
+}
+
 }  // extern "C"

@@ -46,6 +46,16 @@ struct BwdParams {
   float sm_scale;     // 1 / sqrt(D)
 };
 
+// Parameters of the unfused three-kernel baseline (scores, softmax, P V).
+struct UnfParams {
+  void* o;            // [B, H, N, D] output
+  float* s;           // [B, H, N, N] fp32 scores (written by the scores kernel)
+  void* p;            // [B, H, N, N] 16-bit probabilities (written by the softmax kernel)
+  int* status;
+  int N, H, H_kv, group, B;
+  float sm_scale;     // 1 / sqrt(D)
+};
+
 // Work units (heads, head pairs) whose tiles are launched heavy-first together: up to 16 units,
 // about 64 MiB of K/V at S = 8192, D = 128, so the heads in flight keep their K/V in the 126 MB L2.
 inline int work_band(long long units) { return units < 16 ? static_cast<int>(units) : 16; }
@@ -76,6 +86,8 @@ cudaError_t launch_fwd(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUt
                        const FwdParams& p, int D, int block_n, bool bf16, cudaStream_t stream);
 
 cudaError_t launch_bwd_preprocess(const BwdParams& p, bool bf16, cudaStream_t stream);
+cudaError_t launch_unfused(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmP,
+                           const CUtensorMap& tmV, const UnfParams& p, int D, bool bf16, cudaStream_t stream);
 cudaError_t launch_bwd_dkdv(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
                             const CUtensorMap& tmdO, const BwdParams& p, bool bf16,
                             cudaStream_t stream);

@@ -5,7 +5,8 @@
 Input:  .npz with contiguous float16 arrays Q, K, V, each [B, H, N, D];
         1<=B<=16, 1<=H<=32, 1<=N<=32768, D in {32, 64, 128}, N divisible by --block-m and --block-n
 Output: .npy, float16, shape [B, H, N, D]
-Backends: cutile / fused (sm_100a kernel), unfused (not built on B200), reference (PyTorch fp32)
+Backends: cutile / fused (sm_100a kernel), unfused (the three-kernel baseline on sm_100a),
+reference (PyTorch fp32)
 Exit status: 0 success, 2 unsupported input or usage error, 1 runtime failure.
 """
 import os
@@ -24,7 +25,8 @@ def get_backend(name):
         from attention.fused.fused import fused_attention
         return fused_attention
     if name == "unfused":
-        raise NotImplementedError("backend 'unfused' (the reference's 3-kernel cuTile baseline) is not built for B200")
+        from attention.fused.unfused import unfused_attention
+        return lambda q, k, v, bm, bn: unfused_attention(q, k, v, bm, bn)
     if name == "reference":
         from attention.fused.reference import causal_attention_reference
         return lambda q, k, v, bm, bn: causal_attention_reference(q, k, v)

@@ -5,7 +5,8 @@
 Input:  .npz with Q [B, H, N, D], K and V [B, H_kv, N, D] (float16), H_kv dividing H;
         query head h reads K/V head h // (H // H_kv)
 Output: .npy, float16, shape [B, H, N, D]
-Backends: cutile / fused (sm_100a kernel), unfused (not built on B200), reference (PyTorch fp32)
+Backends: cutile / fused (sm_100a kernel), unfused (the three-kernel baseline on sm_100a),
+reference (PyTorch fp32)
 Exit status: 0 success, 2 unsupported input or usage error, 1 runtime failure.
 """
 import os
@@ -24,7 +25,8 @@ def get_backend(name):
         from attention.gqa.fused_gqa import fused_gqa_attention
         return fused_gqa_attention
     if name == "unfused":
-        raise NotImplementedError("backend 'unfused' (the reference's 3-kernel cuTile baseline) is not built for B200")
+        from attention.gqa.unfused_gqa import unfused_gqa_attention
+        return lambda q, k, v, bm, bn: unfused_gqa_attention(q, k, v, bm, bn)
     if name == "reference":
         from attention.gqa.reference_gqa import causal_attention_reference_gqa
         return lambda q, k, v, bm, bn: causal_attention_reference_gqa(q, k, v)

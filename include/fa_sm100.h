@@ -89,6 +89,17 @@ FA_API int fa_bwd_dq(const void* q, const void* k, const void* v, const void* dO
               int B, int H, int H_kv, int S, int D, int dtype, int tile_m, int tile_n,
               int* dev_status, void* stream);
 
+/* Unfused causal forward, the reference's three-kernel baseline: s_buf = causal_mask(q k^T /
+ * sqrt(D)) in float32, p_buf = row_softmax(s_buf) in the dtype of q, o = p_buf v.  Replaces the
+ * three ct.launch calls of attention/fused/unfused.py:96-116 (unfused_attention) and
+ * attention/gqa/unfused_gqa.py:99-128 (unfused_gqa_attention, H_kv < H).  s_buf and p_buf are
+ * caller-owned [B, H, S, S] buffers; only their 128 x 128 tiles on or below the causal diagonal
+ * are written (entries above the diagonal inside those tiles hold -inf and 0).  S % 8 == 0,
+ * B * H <= 65535. */
+FA_API int fa_unfused_fwd(const void* q, const void* k, const void* v, void* o, float* s_buf,
+                          void* p_buf, int B, int H, int H_kv, int S, int D, int dtype,
+                          int* dev_status, void* stream);
+
 /* Whole backward (delta, dk/dv, dq) for callers that cannot allocate device memory: a plugin
  * inside a framework whose memory pool already holds nearly all of HBM, or a latency-critical
  * path that must not call cudaMalloc (it can synchronise the device).  No counterpart in the

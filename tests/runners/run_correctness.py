@@ -6,7 +6,8 @@
 
 For every case of the reference's grids (its 84 MHA and 96 GQA forward cases with their crc32
 seeds, and its 7 backward cases with their CUDA-generator inputs), run the drop-in function
-(`fused_attention`, `fused_gqa_attention`, `fused_attention_autograd`), compare it with the fp32
+(`fused_attention`, `fused_gqa_attention`, `fused_attention_autograd`; with `--impl unfused` the
+three-kernel baseline `unfused_attention` / `unfused_gqa_attention`), compare it with the fp32
 PyTorch ground truth computed on the same device, and write one CSV row per case with the
 reference's columns:
 
@@ -108,6 +109,11 @@ def run_forward(a, device):
             from attention.gqa.fused_gqa import fused_gqa_attention as fn
         else:
             from attention.fused.fused import fused_attention as fn
+    elif a.impl == "unfused":
+        if gqa:
+            from attention.gqa.unfused_gqa import unfused_gqa_attention as fn
+        else:
+            from attention.fused.unfused import unfused_attention as fn
     else:
         fn = lambda q, k, v, tm, tn: reference_forward(q, k, v)  # noqa: E731
     rows, failed = [], 0
@@ -171,6 +177,9 @@ def run_backward(a, device):
 
 def default_csv(a):
     tile = f"{a.tile_m}x{a.tile_n}"
+    if a.impl == "unfused":  # the reference's layout for its non-fused implementations
+        name = "unfused" if a.suite == "fused" else "unfused_gqa"
+        return f"results/correctness/{name}/b200/correctness_{name}_b200_{tile}.csv"
     tag = "b200" if a.impl == "fused" else "reference"
     if a.suite == "fused":
         return f"results/correctness/fused/{tag}/{tile}/correctness_fused_{tag}_{tile}.csv"
@@ -182,7 +191,7 @@ def default_csv(a):
 def main(argv=None):
     p = argparse.ArgumentParser(description="B200 kernels against the fp32 PyTorch ground truth, reference CSV schema")
     p.add_argument("--suite", required=True, choices=("fused", "gqa", "backward"))
-    p.add_argument("--impl", default="fused", choices=("fused", "reference"))
+    p.add_argument("--impl", default="fused", choices=("fused", "unfused", "reference"))
     p.add_argument("--tile-m", type=int, default=64)
     p.add_argument("--tile-n", type=int, default=64)
     p.add_argument("--filter", default="", help="only cases whose id contains this text")
@@ -193,8 +202,10 @@ def main(argv=None):
         device = torch.device(a.device)
         if device.type == "cuda" and not torch.cuda.is_available():
             raise RuntimeError("no CUDA device (use --impl reference --device cpu for a harness self-check)")
-        if a.impl == "fused" and device.type != "cuda":
-            raise RuntimeError("--impl fused needs a CUDA device")
+        if a.impl != "reference" and device.type != "cuda":
+            raise RuntimeError(f"--impl {a.impl} needs a CUDA device")
+        if a.impl == "unfused" and a.suite == "backward":
+            raise RuntimeError("the unfused baseline is forward only")
     except RuntimeError as e:
         print(f"setup error: {e}", file=sys.stderr)
         return 2

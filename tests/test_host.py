@@ -197,9 +197,11 @@ def test_cli_exit_codes(tmp_path):
     good = tmp_path / "good.npz"
     z = np.zeros((1, 2, 128, 64), np.float16)
     np.savez(good, Q=z, K=z[:, :1], V=z[:, :1])
-    rc, err = _cli("run_attention_gqa.py", "--input", str(good), "--output", str(tmp_path / "o.npy"),
-                   "--backend", "unfused")
-    assert rc == 1 and "not built" in err
+    # a runtime failure (here: no GPU visible to the child process) is exit status 1
+    r = subprocess.run([sys.executable, os.path.join(PKG, "run_attention_gqa.py"), "--input", str(good),
+                        "--output", str(tmp_path / "o.npy"), "--backend", "unfused"], capture_output=True,
+                       text=True, env={**os.environ, "CUDA_VISIBLE_DEVICES": ""})
+    assert r.returncode == 1 and "unfused backend failed" in r.stderr and "no CUDA GPU" in r.stderr
 
 
 def test_bench_reference_arm_prints_the_contract_line():
