@@ -9,6 +9,7 @@ calls raise.  Tensors cross the boundary as raw device pointers plus sizes; the 
 torch's current stream, so the kernels order with surrounding torch work exactly like the
 reference's `ct.launch(torch.cuda.current_stream(), ...)` (attention/fused/fused.py:75).
 """
+import contextlib
 import ctypes
 import os
 import threading
@@ -121,6 +122,13 @@ def _raise(rc, what):
     raise RuntimeError(f"{what}: {msg}")  # CUDA, driver or device
 
 
+def _on_device(t):
+    """Make t's device current for the call (a no-op context when it already is)."""
+    if t.device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(t.device)
+
+
 def _ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
 
@@ -141,7 +149,7 @@ def fwd(q, k, v, o, lse, tile_m, tile_n):
     lib = load()
     B, H, S, D = q.shape
     H_kv = k.shape[1]
-    with torch.cuda.device(q.device):
+    with _on_device(q):
         rc = lib.fa_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), B, H, H_kv, S, D,
                         _dtype_code(q), int(tile_m), int(tile_n),
                         _ptr(status_tensor(q.device)), _stream(q))
@@ -152,7 +160,7 @@ def fwd(q, k, v, o, lse, tile_m, tile_n):
 def bwd_preprocess(o, do, delta):
     lib = load()
     B, H, S, D = o.shape
-    with torch.cuda.device(o.device):
+    with _on_device(o):
         rc = lib.fa_bwd_preprocess(_ptr(o), _ptr(do), _ptr(delta), B, H, S, D, _dtype_code(o),
                                    _ptr(status_tensor(o.device)), _stream(o))
     if rc != FA_OK:
@@ -163,7 +171,7 @@ def bwd_dkdv(q, k, v, do, lse, delta, dk, dv, tile_m, tile_n):
     lib = load()
     B, H, S, D = q.shape
     H_kv = k.shape[1]
-    with torch.cuda.device(q.device):
+    with _on_device(q):
         rc = lib.fa_bwd_dkdv(_ptr(q), _ptr(k), _ptr(v), _ptr(do), _ptr(lse), _ptr(delta),
                              _ptr(dk), _ptr(dv), B, H, H_kv, S, D, _dtype_code(q),
                              int(tile_m), int(tile_n), _ptr(status_tensor(q.device)), _stream(q))
@@ -175,7 +183,7 @@ def bwd_dq(q, k, v, do, lse, delta, dq, tile_m, tile_n):
     lib = load()
     B, H, S, D = q.shape
     H_kv = k.shape[1]
-    with torch.cuda.device(q.device):
+    with _on_device(q):
         rc = lib.fa_bwd_dq(_ptr(q), _ptr(k), _ptr(v), _ptr(do), _ptr(lse), _ptr(delta), _ptr(dq),
                            B, H, H_kv, S, D, _dtype_code(q), int(tile_m), int(tile_n),
                            _ptr(status_tensor(q.device)), _stream(q))
@@ -189,7 +197,7 @@ def unfused_fwd(q, k, v, o, s, p):
     lib = load()
     B, H, S, D = q.shape
     H_kv = k.shape[1]
-    with torch.cuda.device(q.device):
+    with _on_device(q):
         rc = lib.fa_unfused_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(s), _ptr(p), B, H, H_kv, S, D,
                                 _dtype_code(q), _ptr(status_tensor(q.device)), _stream(q))
     if rc != FA_OK:
