@@ -168,8 +168,8 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
 }
 
 // P = 2^(S * scale - m) for 32 columns of one row (masked entries, -inf, give 0; the polynomial
-// pairs are only used on tiles without masked entries).  kPoly of the 16 pairs, spread over the chunk, take the
-// polynomial; the rest go to MUFU ex2.
+// pairs are only used on tiles without masked entries).  kPoly of the 16 pairs, spread over the
+// chunk, take the polynomial; the rest go to MUFU ex2.
 template <bool BF16, int kPoly>
 __device__ __forceinline__ void softmax_chunk(const uint32_t (&r)[32], uint64_t scale2, uint64_t negm2,
                                               uint64_t (&sum2)[4], uint32_t (&pk)[16]) {
