@@ -251,7 +251,7 @@ def main():
         group = dist.group.WORLD
 
     from attention.backward.fused_backward import fused_attention_autograd, _forward, _native
-    from attention.dist import sharded_attention_autograd
+    from attention.dist import plan_chunks, sharded_attention_autograd
 
     dt = torch.float16 if a.dtype == "fp16" else torch.bfloat16
     B = a.batch if a.strong else a.batch * world
@@ -301,6 +301,7 @@ def main():
         barrier()
         return max_over_ranks(s.elapsed_time(e))
 
+    launch_chunks = plan_chunks(B * H_kv, world) if world > 1 else 1
     flops_fwd = 2.0 * B * H * S * S * D
     flops_step = 3.5 * flops_fwd
 
@@ -446,7 +447,8 @@ def main():
                 "frac_of_measured_peak": {"fwd+bwd": value / (peak * world), "fwd": fwd_tflops / (peak * world),
                                           "peak_kind": peak_kind},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
-                "gpu_launches": 4 * a.steps}
+                # per step: forward, delta, dK/dV and dQ kernels, once per chunk of this rank's units
+                "gpu_launches": 4 * launch_chunks * a.steps}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
