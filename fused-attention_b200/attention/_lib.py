@@ -122,19 +122,15 @@ def _raise(rc, what):
     raise RuntimeError(f"{what}: {msg}")  # CUDA, driver or device
 
 
-def _on_device(t):
-    """Make t's device current for the call (a no-op context when it already is)."""
-    if t.device.index == torch.cuda.current_device():
-        return contextlib.nullcontext()
-    return torch.cuda.device(t.device)
+# Raw cudaStream_t of a device's current stream without building a torch Stream object (a
+# measurable part of a short call's host time); the public query where torch lacks it.
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
 
 
-def _ptr(t):
-    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
-
-
-def _stream(t):
-    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+def _current_stream(idx):
+    if _RAW_STREAM is not None:
+        return _RAW_STREAM(idx)
+    return torch.cuda.current_stream(idx).cuda_stream
 
 
 def _dtype_code(t):
@@ -144,64 +140,72 @@ def _dtype_code(t):
     return code
 
 
+def _launch(t, calls):
+    """Run the C entry points `calls` [(name, args)] on t's device: each call gets the device's
+    status word and the raw handle of its current stream appended (pointers travel as plain ints,
+    which the c_void_p argtypes convert).  Raises on the first non-zero return code."""
+    lib = load()
+    idx = t.get_device()
+    status = status_tensor(t.device).data_ptr()
+    stream = _current_stream(idx)
+    ctx = contextlib.nullcontext() if idx == torch.cuda.current_device() else torch.cuda.device(idx)
+    with ctx:
+        for name, args in calls:
+            rc = getattr(lib, name)(*args, status, stream)
+            if rc != FA_OK:
+                _raise(rc, name)
+
+
+def _p(t):
+    return t.data_ptr() if t is not None else None
+
+
 def fwd(q, k, v, o, lse, tile_m, tile_n):
     """Enqueue the forward kernel: o (and lse if not None) from q, k, v (all contiguous CUDA)."""
-    lib = load()
     B, H, S, D = q.shape
-    H_kv = k.shape[1]
-    with _on_device(q):
-        rc = lib.fa_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), B, H, H_kv, S, D,
-                        _dtype_code(q), int(tile_m), int(tile_n),
-                        _ptr(status_tensor(q.device)), _stream(q))
-    if rc != FA_OK:
-        _raise(rc, "fa_fwd")
+    _launch(q, [("fa_fwd", (q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), _p(lse), B, H, k.shape[1],
+                            S, D, _dtype_code(q), int(tile_m), int(tile_n)))])
 
 
 def bwd_preprocess(o, do, delta):
-    lib = load()
     B, H, S, D = o.shape
-    with _on_device(o):
-        rc = lib.fa_bwd_preprocess(_ptr(o), _ptr(do), _ptr(delta), B, H, S, D, _dtype_code(o),
-                                   _ptr(status_tensor(o.device)), _stream(o))
-    if rc != FA_OK:
-        _raise(rc, "fa_bwd_preprocess")
+    _launch(o, [("fa_bwd_preprocess", (o.data_ptr(), do.data_ptr(), delta.data_ptr(), B, H, S, D, _dtype_code(o)))])
+
+
+def _dkdv_args(q, k, v, do, lse, delta, dk, dv, tile_m, tile_n):
+    B, H, S, D = q.shape
+    return (q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(), delta.data_ptr(),
+            dk.data_ptr(), dv.data_ptr(), B, H, k.shape[1], S, D, _dtype_code(q), int(tile_m), int(tile_n))
+
+
+def _dq_args(q, k, v, do, lse, delta, dq, tile_m, tile_n):
+    B, H, S, D = q.shape
+    return (q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(), delta.data_ptr(),
+            dq.data_ptr(), B, H, k.shape[1], S, D, _dtype_code(q), int(tile_m), int(tile_n))
 
 
 def bwd_dkdv(q, k, v, do, lse, delta, dk, dv, tile_m, tile_n):
-    lib = load()
-    B, H, S, D = q.shape
-    H_kv = k.shape[1]
-    with _on_device(q):
-        rc = lib.fa_bwd_dkdv(_ptr(q), _ptr(k), _ptr(v), _ptr(do), _ptr(lse), _ptr(delta),
-                             _ptr(dk), _ptr(dv), B, H, H_kv, S, D, _dtype_code(q),
-                             int(tile_m), int(tile_n), _ptr(status_tensor(q.device)), _stream(q))
-    if rc != FA_OK:
-        _raise(rc, "fa_bwd_dkdv")
+    _launch(q, [("fa_bwd_dkdv", _dkdv_args(q, k, v, do, lse, delta, dk, dv, tile_m, tile_n))])
 
 
 def bwd_dq(q, k, v, do, lse, delta, dq, tile_m, tile_n):
-    lib = load()
-    B, H, S, D = q.shape
-    H_kv = k.shape[1]
-    with _on_device(q):
-        rc = lib.fa_bwd_dq(_ptr(q), _ptr(k), _ptr(v), _ptr(do), _ptr(lse), _ptr(delta), _ptr(dq),
-                           B, H, H_kv, S, D, _dtype_code(q), int(tile_m), int(tile_n),
-                           _ptr(status_tensor(q.device)), _stream(q))
-    if rc != FA_OK:
-        _raise(rc, "fa_bwd_dq")
+    _launch(q, [("fa_bwd_dq", _dq_args(q, k, v, do, lse, delta, dq, tile_m, tile_n))])
+
+
+def bwd(q, k, v, o, do, lse, delta, dq, dk, dv, tile_m, tile_n):
+    """The whole backward: delta, then dK/dV, then dQ, enqueued in one go."""
+    B, H, S, D = o.shape
+    _launch(q, [("fa_bwd_preprocess", (o.data_ptr(), do.data_ptr(), delta.data_ptr(), B, H, S, D, _dtype_code(o))),
+                ("fa_bwd_dkdv", _dkdv_args(q, k, v, do, lse, delta, dk, dv, tile_m, tile_n)),
+                ("fa_bwd_dq", _dq_args(q, k, v, do, lse, delta, dq, tile_m, tile_n))])
 
 
 def unfused_fwd(q, k, v, o, s, p):
     """Enqueue the unfused three-kernel forward: s (fp32 [B, H, N, N]) = masked scaled scores,
     p (dtype of q, [B, H, N, N]) = row softmax, o = p v."""
-    lib = load()
     B, H, S, D = q.shape
-    H_kv = k.shape[1]
-    with _on_device(q):
-        rc = lib.fa_unfused_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(s), _ptr(p), B, H, H_kv, S, D,
-                                _dtype_code(q), _ptr(status_tensor(q.device)), _stream(q))
-    if rc != FA_OK:
-        _raise(rc, "fa_unfused_fwd")
+    _launch(q, [("fa_unfused_fwd", (q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), s.data_ptr(),
+                                    p.data_ptr(), B, H, k.shape[1], S, D, _dtype_code(q)))])
 
 
 def load_by_path():

@@ -80,8 +80,10 @@ def _backward_q(q, k, v, do, lse, delta, tile_m, tile_n, dq=None):
 
 
 def _backward(q, k, v, o, lse, do, tile_m, tile_n):
-    delta, dk, dv = _backward_kv(q, k, v, o, lse, do, tile_m, tile_n)
-    dq = _backward_q(q, k, v, do, lse, delta, tile_m, tile_n)
+    B, H, N, D = q.shape
+    delta = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    _native().bwd(q, k, v, o, do, lse, delta, dq, dk, dv, tile_m, tile_n)  # delta, dK/dV, dQ
     return dq, dk, dv
 
 
