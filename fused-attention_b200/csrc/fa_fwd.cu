@@ -49,9 +49,16 @@ constexpr int kBM = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only if the max grows > 256x
 
-#ifndef FA_FWD_POLY_PAIRS
-#define FA_FWD_POLY_PAIRS 2  // of every 16 exp2 pairs, this many go to the FMA-pipe polynomial
+// Of every 16 exp2 pairs on interior tiles, this many go to the FMA-pipe polynomial (measured
+// best: 3 with 128-key tiles, +2 % over 2, while 4 and 5 are slower; 1 with 64-key tiles).
+template <int BN>
+constexpr int poly_pairs() {
+#ifdef FA_FWD_POLY_PAIRS
+  return FA_FWD_POLY_PAIRS;
+#else
+  return BN == 128 ? 3 : 1;
 #endif
+}
 
 template <int D, int BN>
 struct FwdCfg {
@@ -504,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = 0; c < NCH / 2; ++c) {
             uint32_t pk[16];
-            softmax_chunk<BF16, FA_FWD_POLY_PAIRS>(r[c], scale2, negm2, sum2, pk);
+            softmax_chunk<BF16, poly_pairs<BN>()>(r[c], scale2, negm2, sum2, pk);
             tmem_st16(tS + c * 16, pk);
           }
           const float mt = row_max<NCH>(r) * scale;
@@ -530,7 +537,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = NCH / 2; c < NCH; ++c) {
             uint32_t pk[16];
-            softmax_chunk<BF16, FA_FWD_POLY_PAIRS>(r[c], scale2, negm2, sum2, pk);
+            softmax_chunk<BF16, poly_pairs<BN>()>(r[c], scale2, negm2, sum2, pk);
             tmem_st16(tS + c * 16, pk);
           }
           tmem_st_wait();
