@@ -76,16 +76,32 @@ constexpr int kBT = 128;  // tile rows (outer and inner)
 constexpr uint32_t kBwdTmemCols = 512;
 constexpr int kSmemOptin = 232448;  // max dynamic shared memory per block on sm_100
 
-// P = 2^(s * scale - m) for kN values (m given per pair), fp32 results, every exp2 on MUFU ex2
-// (an FMA-pipe polynomial for part of them measured 3-8 % slower: these phases are bound by
-// their instruction stream, not by MUFU throughput).
-template <int kN>
+// Of every 16 exp2 pairs, this many go to the FMA-pipe polynomial: 2 in the dK/dV kernel (3 %
+// faster than none; it runs at the power cap, and the polynomial costs less energy than MUFU work),
+// none in the dQ kernel (2 % slower with one or two).
+#ifndef FA_DKDV_POLY_PAIRS
+#define FA_DKDV_POLY_PAIRS 2
+#endif
+#ifndef FA_DQ_POLY_PAIRS
+#define FA_DQ_POLY_PAIRS 0
+#endif
+
+// True for the polynomial pairs of a 16-pair group, spread evenly (none when kPoly == 0).
+template <int kPoly>
+__device__ __forceinline__ constexpr bool poly_pair(int i) {
+  return kPoly > 0 && (i % 16) % (16 / (kPoly > 0 ? kPoly : 1)) == (16 / (kPoly > 0 ? kPoly : 1)) - 1;
+}
+
+// P = 2^(s * scale - m) for kN values (m given per pair), fp32 results, exp2 on MUFU ex2 except
+// kPoly of every 16 pairs on the FMA-pipe polynomial.
+template <int kN, int kPoly>
 __device__ __forceinline__ void exp2_row(const uint32_t* s, const float* neg_m, float scale, float* out) {
   const uint64_t scale2 = f2(scale, scale);
 #pragma unroll
   for (int i = 0; i < kN / 2; ++i) {
     const uint64_t x2 = ffma2(f2u(s[2 * i], s[2 * i + 1]), scale2, f2(neg_m[2 * i], neg_m[2 * i + 1]));
-    const uint64_t p2 = f2(ex2_approx(f2lo(x2)), ex2_approx(f2hi(x2)));
+    const uint64_t p2 = poly_pair<kPoly>(i) ? exp2_poly2(x2)
+                                                         : f2(ex2_approx(f2lo(x2)), ex2_approx(f2hi(x2)));
     out[2 * i] = f2lo(p2);
     out[2 * i + 1] = f2hi(p2);
   }
@@ -93,8 +109,9 @@ __device__ __forceinline__ void exp2_row(const uint32_t* s, const float* neg_m, 
 
 // P = 2^(s * scale - lse) for kN values with a per-value lse (read as float4 from shared memory,
 // so each (x, y) / (z, w) half is a ready register pair): y = lse - s * scale in one packed FMA and
-// 2^(-y), so no per-value negation is needed.
-template <int kN>
+// 2^(-y) on MUFU, so no per-value negation is needed; kPoly of every 16 pairs instead take the
+// FMA-pipe polynomial of x = -y.
+template <int kN, int kPoly>
 __device__ __forceinline__ void exp2_row_lse(const uint32_t* s, const float* lse, float scale, float* out) {
   const uint64_t nscale2 = f2(-scale, -scale);
 #pragma unroll
@@ -102,10 +119,22 @@ __device__ __forceinline__ void exp2_row_lse(const uint32_t* s, const float* lse
     const float4 l4 = *reinterpret_cast<const float4*>(lse + c);
     const uint64_t y0 = ffma2(f2u(s[c], s[c + 1]), nscale2, f2(l4.x, l4.y));
     const uint64_t y1 = ffma2(f2u(s[c + 2], s[c + 3]), nscale2, f2(l4.z, l4.w));
-    out[c] = ex2_neg_approx(f2lo(y0));
-    out[c + 1] = ex2_neg_approx(f2hi(y0));
-    out[c + 2] = ex2_neg_approx(f2lo(y1));
-    out[c + 3] = ex2_neg_approx(f2hi(y1));
+    if (poly_pair<kPoly>(c / 2)) {
+      const uint64_t p2 = exp2_poly2(fsub2(0ull, y0));
+      out[c] = f2lo(p2);
+      out[c + 1] = f2hi(p2);
+    } else {
+      out[c] = ex2_neg_approx(f2lo(y0));
+      out[c + 1] = ex2_neg_approx(f2hi(y0));
+    }
+    if (poly_pair<kPoly>(c / 2 + 1)) {
+      const uint64_t p2 = exp2_poly2(fsub2(0ull, y1));
+      out[c + 2] = f2lo(p2);
+      out[c + 3] = f2hi(p2);
+    } else {
+      out[c + 2] = ex2_neg_approx(f2lo(y1));
+      out[c + 3] = ex2_neg_approx(f2hi(y1));
+    }
   }
 }
 
@@ -415,8 +444,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       mbar_arrive(BAR(DQ_SFREE));
       float pr[64];
-      exp2_row<32>(sv[0], neg_lse, p.scale_log2, pr);
-      exp2_row<32>(sv[1], neg_lse, p.scale_log2, pr + 32);
+      exp2_row<32, FA_DQ_POLY_PAIRS>(sv[0], neg_lse, p.scale_log2, pr);
+      exp2_row<32, FA_DQ_POLY_PAIRS>(sv[1], neg_lse, p.scale_log2, pr + 32);
       const int k0 = s * kBT + 64 * w;
       if (k0 + 63 > i * kBT || k0 + 64 > p.S) {
 #pragma unroll
@@ -676,8 +705,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const float* lse = reinterpret_cast<const float*>(sm.ptr + C::kOffLse + qs * C::kStat) + 64 * w;
       const float* del = reinterpret_cast<const float*>(sm.ptr + C::kOffDelta + os * C::kStat) + 64 * w;
       float pr[64];
-      exp2_row_lse<32>(sv[0], lse, scale, pr);
-      exp2_row_lse<32>(sv[1], lse + 32, scale, pr + 32);
+      exp2_row_lse<32, FA_DKDV_POLY_PAIRS>(sv[0], lse, scale, pr);
+      exp2_row_lse<32, FA_DKDV_POLY_PAIRS>(sv[1], lse + 32, scale, pr + 32);
       const int q0 = it * kBT + 64 * w;
       if (key > q0 || q0 + 64 > p.S) {  // some query of these 64 precedes the key, or lies past S
 #pragma unroll

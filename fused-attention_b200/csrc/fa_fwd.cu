@@ -150,30 +150,6 @@ __device__ __forceinline__ Work decode_work(const FwdParams& p, int item) {
   return w;
 }
 
-// 2^x for a pair of x <= 0 on the FMA pipe (no MUFU): x = n + f with n = round(x) (the 1.5 * 2^23
-// addition leaves n in the low mantissa bits) and f in [-1/2, 1/2]; 2^f by a degree-3 polynomial
-// fitted here to 2^f on [-1/2, 1/2] (relative-error least squares on Chebyshev nodes, reweighted
-// towards the worst points: max relative error 7.5e-5, below half an fp16 ulp); 2^n is added to
-// the result's exponent field.  x is clamped at -125 first: the polynomial's value lies in
-// [2^-1/2, 2^1/2], so its exponent field is 126 or 127 and stays >= 1 (a normal number) after
-// adding n >= -125.  Scores that far below the row maximum give at most 2^-124 instead of ~0,
-// below anything a 16-bit P or the fp32 row sum can resolve next to the row's largest term (1).
-__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
-  const float x0 = fmaxf(f2lo(x2), -125.f), x1 = fmaxf(f2hi(x2), -125.f);
-  const uint64_t xc = f2(x0, x1);
-  const uint64_t magic = f2(12582912.f, 12582912.f);
-  const uint64_t j = fadd2(xc, magic);
-  const uint64_t n = fsub2(j, magic);
-  const uint64_t f = fsub2(xc, n);
-  uint64_t p = ffma2(f2(0.05517164617776871f, 0.05517164617776871f), f,
-                     f2(0.24261116981506348f, 0.24261116981506348f));
-  p = ffma2(p, f, f2(0.6932609677314758f, 0.6932609677314758f));
-  p = ffma2(p, f, f2(0.9999280571937561f, 0.9999280571937561f));
-  const uint32_t lo = static_cast<uint32_t>(p) + (static_cast<uint32_t>(j) << 23);
-  const uint32_t hi = static_cast<uint32_t>(p >> 32) + (static_cast<uint32_t>(j >> 32) << 23);
-  return f2u(lo, hi);
-}
-
 // P = 2^(S * scale - m) for 32 columns of one row (masked entries, -inf, give 0; the polynomial
 // pairs are only used on tiles without masked entries).  kPoly of the 16 pairs, spread over the
 // chunk, take the polynomial; the rest go to MUFU ex2.

@@ -1,4 +1,4 @@
-"""CPU restatement of the forward kernel's FMA-pipe exp2 (fa_fwd.cu: exp2_poly2), checked in
+"""CPU restatement of the kernels' FMA-pipe exp2 (fa_sm100.cuh: exp2_poly2), checked in
 float32 over its whole input range.
 
 The kernel evaluates part of each softmax row's 2^x (x <= 0, or up to the rescale threshold above
@@ -13,7 +13,7 @@ import re
 import numpy as np
 
 SRC = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
-                   "fused-attention_b200", "csrc", "fa_fwd.cu")
+                   "fused-attention_b200", "csrc", "fa_sm100.cuh")
 
 
 def _kernel_constants():
