@@ -23,6 +23,12 @@
 //               S_t = Q_t K_j^T into TMEM, O_t += P_t V_j with P_t read from TMEM
 //   warp 10     TMA producer: the V ring
 //   warp 11     idle
+// Registers: the launch gives every thread 168; with 128-key tiles the producer/issuer warpgroup
+// (warps 8-11) drops to 104 and the two softmax warpgroups, which hold 128 scores per thread, rise
+// to 200 (4 x 32 x 104 + 8 x 32 x 200 = 384 x 168; neither side spills).  These are the only two
+// budget changes: the increases can only be met from what the decrease frees, so nothing else may
+// claim registers (a warp that raised its budget again at its end could take them first and leave
+// a softmax warp waiting forever).  The teardown after the role branches runs under both budgets.
 // TMEM (512 columns): S_0 | S_1 | O_0 | O_1, 128 columns each; P_t (16-bit) overwrites the first
 // BN/2 columns of S_t once the row is in registers.  The two tiles ping-pong: while one tile's
 // warpgroup turns S into P, the tensor core runs the other tile's P V and next Q K^T.  P is
@@ -48,6 +54,22 @@ constexpr int kWarpProducerV = 10;  // the V ring
 constexpr int kBM = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only if the max grows > 256x
+constexpr int kLaunchRegs = 168;           // 65536 / 384, rounded down to the allocation unit of 8
+constexpr int kRegsSoftmax = 200;
+constexpr int kRegsOther = 104;
+static_assert(4 * 32 * kRegsOther + 8 * 32 * kRegsSoftmax <= kThreads * kLaunchRegs, "register split");
+constexpr int kSoftmaxCopy = 1;  // the softmax warpgroups' own copy of the bounded-wait loop
+
+// Register split between the warpgroups: with 128-key tiles (a softmax thread holds 128 scores,
+// and 168 registers spill).
+template <int BN>
+constexpr bool reg_split() {
+#ifdef FA_FWD_REG_SPLIT
+  return FA_FWD_REG_SPLIT != 0 && BN == 128;
+#else
+  return BN == 128;
+#endif
+}
 
 // Of every 16 exp2 pairs on interior tiles, this many go to the FMA-pipe polynomial (measured
 // best: 3 with 128-key tiles, +2 % over 2, while 4 and 5 are slower; 1 with 64-key tiles).
@@ -294,6 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp >= kSoftmaxWarps) {
+  if constexpr (reg_split<BN>()) regs_decrease<kRegsOther>();
   if (warp == kWarpProducerK) {
     // ------------------------------------------------------------ TMA: Q once, then the K ring
     if (lane == 0) {
@@ -420,6 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ softmax / epilogue
     // warpgroup t serves query tile t; a thread owns one row (TMEM lane) and its BN scores.
+    if constexpr (reg_split<BN>()) regs_increase<kRegsSoftmax>();
     const int t = warp / 4;
     if (t < w.ntiles) {
       constexpr int NCH = BN / 32;  // 32-column chunks of a row
@@ -436,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float l = 0.f;
       bool ok = true;
       for (int j = 0; j < nkv; ++j) {
-        if (!(ok = warp_all(mbar_wait(BAR(BAR_SFULL + t), j & 1, p.status, kDevTimeoutS)))) break;
+        if (!(ok = warp_all(mbar_wait<kSoftmaxCopy>(BAR(BAR_SFULL + t), j & 1, p.status, kDevTimeoutS)))) break;
         tc_fence_after();
         uint32_t r[NCH][32];
 #pragma unroll
@@ -523,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t s01 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
         l = l * alpha + (f2lo(s01) + f2hi(s01));
       }
-      if (ok) ok = mbar_wait(BAR(BAR_OFULL + t), 0, p.status, kDevTimeoutO);
+      if (ok) ok = mbar_wait<kSoftmaxCopy>(BAR(BAR_OFULL + t), 0, p.status, kDevTimeoutO);
       ok = warp_all(ok);
       if (ok) {
         tc_fence_after();
@@ -566,7 +590,7 @@ cudaError_t launch_fwd_t(const CUtensorMap& tmQ, const CUtensorMap& tmK, const C
   using C = FwdCfg<D, BN>;
   auto kern = fa_fwd_kernel<D, BN, BF16>;
   static std::atomic<bool> smem_set[64];
-  cudaError_t e = opt_in_smem(kern, C::kSmemBytes, smem_set);
+  cudaError_t e = opt_in_smem(kern, C::kSmemBytes, smem_set, reg_split<BN>() ? kLaunchRegs : 0);
   if (e != cudaSuccess) return e;
   kern<<<p.n_items, kThreads, C::kSmemBytes, stream>>>(tmQ, tmK, tmV, p);
   return cudaGetLastError();

@@ -64,11 +64,20 @@ inline int work_band(long long units) { return units < 16 ? static_cast<int>(uni
 // per-function, per-device setting; setting it on every launch costs host time on short calls).
 // `done` is the kernel's own flag array; devices past its size set the attribute every time.
 template <typename Kernel>
-inline cudaError_t opt_in_smem(Kernel kernel, int bytes, std::atomic<bool> (&done)[64]) {
+inline cudaError_t opt_in_smem(Kernel kernel, int bytes, std::atomic<bool> (&done)[64],
+                               int launch_regs = 0) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 0 && dev < 64 && done[dev].load(std::memory_order_acquire)) return cudaSuccess;
+  if (launch_regs > 0) {
+    // A kernel that moves registers between its warpgroups at run time was written for exactly
+    // this many registers per thread at launch; with fewer, its increases could never be met.
+    cudaFuncAttributes attr;
+    e = cudaFuncGetAttributes(&attr, kernel);
+    if (e != cudaSuccess) return e;
+    if (attr.numRegs != launch_regs) return cudaErrorInvalidKernelImage;
+  }
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev].store(true, std::memory_order_release);
   return e;

@@ -117,7 +117,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Wait until the phase with the given parity has completed.  Returns false (after recording
 // `code` in the status word, unless another CTA already failed) if the wait exceeds
 // FA_WAIT_TIMEOUT_NS or if the status word shows that some CTA has already failed.
-// The already-complete case is inlined; only a real wait calls the polling loop.
+// The already-complete case is inlined; only a real wait calls the polling loop.  kCopy selects
+// one of several identical copies of the loop: a kernel whose warpgroups run under different
+// register budgets gives each budget its own copy (one callee cannot serve two budgets).
+template <int kCopy = 0>
 static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, int* status,
                                                    int code) {
   const uint64_t t0 = global_timer_ns();
@@ -133,9 +136,10 @@ static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity
   }
 }
 
+template <int kCopy = 0>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* status, int code) {
   if (mbar_try_wait(bar, parity)) return true;
-  return mbar_wait_slow(bar, parity, status, code);
+  return mbar_wait_slow<kCopy>(bar, parity, status, code);
 }
 
 // Bounded wait used only while tearing down: ignores the abort flag so that copies and MMAs
@@ -211,6 +215,20 @@ __device__ __forceinline__ void tc_fence_before() {
 }
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Per-warpgroup register budgets (every warp of a warpgroup executes the same instruction).  The
+// increases draw on the registers the block was launched with: the budgets of all warpgroups
+// must add up to at most threads x registers per thread at launch, which the launch checks.
+template <int N>
+__device__ __forceinline__ void regs_increase() {
+  static_assert(N % 8 == 0 && N >= 24 && N <= 256, "register budget");
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_decrease() {
+  static_assert(N % 8 == 0 && N >= 24 && N <= 256, "register budget");
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // ---------------------------------------------------------------- tcgen05: descriptors

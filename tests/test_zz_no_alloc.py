@@ -10,7 +10,9 @@ point keeps that scratch in a fixed-size static device array inside the library 
 The GPU test calls it through the C ABI twice in a row, with different shapes and dtypes (so a
 stale scratch from the first call would show), and compares dQ, dK, dV with the regular
 three-call backward (fa_bwd_preprocess, fa_bwd_dkdv, fa_bwd_dq) that uses a caller-allocated
-delta.  This file is named to be collected last.
+delta.  A second GPU test captures the entry point into a CUDA graph on a side stream (after one
+uncaptured call, as the header requires) and checks that replays write the same bits as uncaptured
+calls, also after the inputs change in place.  This file is named to be collected last.
 """
 import ctypes
 
@@ -74,6 +76,51 @@ def test_noalloc_backward_matches_regular_backward_twice(cuda_device):
             err = ((got.float() - ref.float()).abs() / (ATOL + RTOL * ref.float().abs())).max().item()
             assert err <= 1.0, (call, name, err)
             assert torch.equal(got, ref), (call, name)  # same kernels, same inputs: identical bits
+
+
+@pytest.mark.gpu
+def test_noalloc_backward_replays_from_a_cuda_graph(cuda_device):
+    nat = _nat()
+    lib = nat.load()
+    B, H, H_kv, S, D, tm, tn = 2, 4, 2, 512, 128, 64, 128
+    g = torch.Generator(device=cuda_device).manual_seed(7)
+    q, do = (torch.randn(B, H, S, D, device=cuda_device, generator=g).half() for _ in range(2))
+    k, v = (torch.randn(B, H_kv, S, D, device=cuda_device, generator=g).half() for _ in range(2))
+    o = torch.empty_like(q)
+    lse = torch.empty(B, H, S, device=cuda_device, dtype=torch.float32)
+    nat.fwd(q, k, v, o, lse, tm, tn)
+    status = nat.status_tensor(cuda_device)
+    main = torch.cuda.current_stream(cuda_device)
+
+    def eager():
+        outs = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v))
+        rc = _call_noalloc(lib, q, k, v, o, do, lse, *outs, tm, tn, status, main.cuda_stream)
+        assert rc == FA_OK, lib.fa_strerror(rc).decode()
+        nat.check_status(cuda_device)
+        return outs
+
+    ref = eager()  # the uncaptured call that must precede capture in this context
+    dq, dk, dv = torch.full_like(q, 7.0), torch.full_like(k, 7.0), torch.full_like(v, 7.0)
+    side = torch.cuda.Stream(cuda_device)
+    side.wait_stream(main)
+    graph = torch.cuda.CUDAGraph()
+    rcs = []
+    with torch.cuda.graph(graph, stream=side):
+        rcs.append(_call_noalloc(lib, q, k, v, o, do, lse, dq, dk, dv, tm, tn, status, side.cuda_stream))
+    assert rcs == [FA_OK], lib.fa_strerror(rcs[0]).decode()
+    torch.cuda.synchronize(cuda_device)
+    assert bool((dq == 7.0).all())  # capture records the launches without running them
+    for replay in range(2):
+        if replay == 1:  # new inputs in the same buffers: the graph reads them, the scratch is reused
+            do.copy_(torch.randn(do.shape, device=cuda_device, generator=g).half())
+            o.mul_(-1.0)
+            ref = eager()
+        graph.replay()
+        torch.cuda.synchronize(cuda_device)
+        nat.check_status(cuda_device)
+        for name, got, r in zip(("dQ", "dK", "dV"), (dq, dk, dv), ref):
+            assert torch.equal(got, r), (replay, name)
+    del graph
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch():
