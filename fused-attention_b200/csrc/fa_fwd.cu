@@ -72,13 +72,13 @@ constexpr bool reg_split() {
 }
 
 // Of every 16 exp2 pairs on interior tiles, this many go to the FMA-pipe polynomial (measured
-// best: 3 with 128-key tiles, +2 % over 2, while 4 and 5 are slower; 1 with 64-key tiles).
+// best: 4 with 128-key tiles and the register split, +1-3 % over 3; 1 with 64-key tiles).
 template <int BN>
 constexpr int poly_pairs() {
 #ifdef FA_FWD_POLY_PAIRS
   return FA_FWD_POLY_PAIRS;
 #else
-  return BN == 128 ? 3 : 1;
+  return BN == 128 ? 4 : 1;
 #endif
 }
 
