@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--tile-m", type=int, default=64)
     ap.add_argument("--tile-n", type=int, default=128)
     ap.add_argument("--e2e-steps", type=int, default=None, help="default: --steps")
+    ap.add_argument("--e2e-slices", type=int, default=32,
+                    help="pipeline slices per end-to-end step on one GPU (upper bound)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     a = ap.parse_args()
     c5 = a.workload == "c5"
@@ -373,39 +375,42 @@ def main():
     hdk = torch.empty(k.shape, dtype=dt).pin_memory()
     hdv = torch.empty(v.shape, dtype=dt).pin_memory()
 
-    # The host-resident job streams through the public API one batch slice at a time (attention
-    # is independent per batch entry): slice c+1 copies in on one stream while slice c computes
-    # and slice c-1 copies out on another (PCIe is full duplex).  Every byte of Q, K, V, dO goes
-    # in and every byte of O, dQ, dK, dV comes out inside the timed region.  A slice is `world`
-    # batch entries, so with N GPUs each rank still gets a full share of every call; on one GPU
-    # with MHA each batch entry is cut into head groups (contiguous, independent) so that a step
-    # has about 16 slices: that shortens the copy-in of the first slice and the copy-out of the
-    # last, the parts no compute can hide (the PCIe copies, not the kernels, bound this leg).
+    # The host-resident job streams through the public API one slice at a time (attention is
+    # independent per batch entry and per K/V head with its query-head group): slice c+1 copies in
+    # on one stream while slice c computes and slice c-1 copies out on another (PCIe is full
+    # duplex).  Every byte of Q, K, V, dO goes in and every byte of O, dQ, dK, dV comes out inside
+    # the timed region.  A slice is `world` batch entries, so with N GPUs each rank still gets a
+    # full share of every call; on one GPU each batch entry is also cut into runs of whole K/V-head
+    # groups (contiguous in every tensor), up to --e2e-slices slices per step: small slices shorten
+    # the copy-in of the first slice and the copy-out of the last, the parts no compute can hide
+    # (the PCIe copies, not the kernels, bound this leg).
     h2d_stream = torch.cuda.Stream(device=dev)
     d2h_stream = torch.cuda.Stream(device=dev)
     comp = torch.cuda.current_stream(dev)
     bs = world
     hsplit = 1
-    if world == 1 and H_kv == H:
-        while hsplit * 2 * (B // bs) <= 16 and H % (hsplit * 2) == 0:
+    if world == 1:
+        while hsplit * 2 * (B // bs) <= a.e2e_slices and H_kv % (hsplit * 2) == 0:
             hsplit *= 2
-    hh = H // hsplit
-    slices = [(slice(c * bs, (c + 1) * bs), slice(p * hh, (p + 1) * hh))
+    kvh = H_kv // hsplit
+    qh = kvh * (H // H_kv)
+    slices = [((slice(c * bs, (c + 1) * bs), slice(p * qh, (p + 1) * qh)),
+               (slice(c * bs, (c + 1) * bs), slice(p * kvh, (p + 1) * kvh)))
               for c in range(B // bs) for p in range(hsplit)]
     nslices = len(slices)
 
     def e2e_step():
         h2d_stream.wait_stream(comp)
         ins = []
-        for sb, sh in slices:
-            sl = (sb, sh) if hsplit > 1 else (sb,)
+        for slq, slk in slices:
             with torch.cuda.stream(h2d_stream):
-                tens = [t[sl].to(dev, non_blocking=True) for t in (hq, hk, hv, hdo)]
+                tens = [hq[slq].to(dev, non_blocking=True), hk[slk].to(dev, non_blocking=True),
+                        hv[slk].to(dev, non_blocking=True), hdo[slq].to(dev, non_blocking=True)]
                 ready = torch.cuda.Event()
                 ready.record(h2d_stream)
-            ins.append((sl, tens, ready))
+            ins.append((slq, slk, tens, ready))
         keep = []
-        for sl, (tq, tk, tv, tdo), ready in ins:
+        for slq, slk, (tq, tk, tv, tdo), ready in ins:
             comp.wait_event(ready)
             q_, k_, v_ = (t.requires_grad_(True) for t in (tq, tk, tv))
             o = attn(q_, k_, v_)
@@ -414,10 +419,10 @@ def main():
             done.record(comp)
             with torch.cuda.stream(d2h_stream):
                 d2h_stream.wait_event(done)
-                ho[sl].copy_(o.detach(), non_blocking=True)
-                hdq[sl].copy_(q_.grad, non_blocking=True)
-                hdk[sl].copy_(k_.grad, non_blocking=True)
-                hdv[sl].copy_(v_.grad, non_blocking=True)
+                ho[slq].copy_(o.detach(), non_blocking=True)
+                hdq[slq].copy_(q_.grad, non_blocking=True)
+                hdk[slk].copy_(k_.grad, non_blocking=True)
+                hdv[slk].copy_(v_.grad, non_blocking=True)
             keep.append((tq, tk, tv, tdo, o))  # no buffer is reused before the copies end
         comp.wait_stream(d2h_stream)
 
