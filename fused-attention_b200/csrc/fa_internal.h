@@ -58,7 +58,12 @@ struct UnfParams {
 
 // Work units (heads, head pairs) whose tiles are launched heavy-first together: up to 16 units,
 // about 64 MiB of K/V at S = 8192, D = 128, so the heads in flight keep their K/V in the 126 MB L2.
-inline int work_band(long long units) { return units < 16 ? static_cast<int>(units) : 16; }
+#ifndef FA_WORK_BAND
+#define FA_WORK_BAND 16
+#endif
+inline int work_band(long long units) {
+  return units < FA_WORK_BAND ? static_cast<int>(units) : FA_WORK_BAND;
+}
 
 // Opt a kernel into `bytes` of dynamic shared memory once per device (the attribute is a
 // per-function, per-device setting; setting it on every launch costs host time on short calls).
