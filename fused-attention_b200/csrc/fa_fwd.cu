@@ -30,7 +30,8 @@
 // claim registers (a warp that raised its budget again at its end could take them first and leave
 // a softmax warp waiting forever).  The teardown after the role branches runs under both budgets.
 // TMEM (512 columns): S_0 | S_1 | O_0 | O_1, 128 columns each; P_t (16-bit) overwrites the first
-// BN/2 columns of S_t once the row is in registers.  The two tiles ping-pong: while one tile's
+// BN/2 columns of S_t once the row is in registers.  With 64-key tiles S_t takes 64 of the tile's
+// 128 columns, so each tile has two S buffers and Q K^T runs two steps ahead of P V.  The two tiles ping-pong: while one tile's
 // warpgroup turns S into P, the tensor core runs the other tile's P V and next Q K^T.  P is
 // published in two halves (keys [0, BN/2) and [BN/2, BN)), so the first half's P V runs while the
 // second half is exponentiated; on interior tiles the first half uses the running max, and the
@@ -121,8 +122,18 @@ enum : int {
   BAR_DRAIN = 23,
   BAR_PFULLB = 24,  // + tile (2): P of the second half
   BAR_NEVER = 26,   // never arrived at (the failure-detection test build waits on it)
-  BAR_COUNT = 27
+  BAR_SFULLB = 27,  // + tile (2): S in the tile's second buffer (64-key tiles)
+  BAR_PVDONE = 29,  // + tile (2): the tile's P V of the step is done (64-key tiles)
+  BAR_COUNT = 31
 };
+
+// 64-key tiles: S takes 64 of a tile's 128 TMEM columns, so each tile keeps two S buffers and the
+// issuer runs Q K^T two steps ahead (S(j+2) into the buffer that P(j) V just read): the softmax
+// warpgroup finds S(j+1) ready when it finishes P(j).
+template <int BN>
+constexpr bool s_double() {
+  return BN == 64;
+}
 
 struct QTile {
   int bh;  // b * H + h (query head)
@@ -298,6 +309,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(BAR(BAR_SFULL + t), 1);
+      mbar_init(BAR(BAR_SFULLB + t), 1);
+      mbar_init(BAR(BAR_PVDONE + t), 1);
       mbar_init(BAR(BAR_PFULLA + t), 128);
       mbar_init(BAR(BAR_PFULLB + t), 128);
       mbar_init(BAR(BAR_OFULL + t), 1);
@@ -371,68 +384,157 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dv0 = sdesc_sw(sV, C::kKVChunkBytes, C::kSbo, C::kLayout);
       const uint32_t tS0 = tmem, tS1 = tmem + 128, tO0 = tmem + 256, tO1 = tmem + 384;
       const int n0 = w.nkv[0], n1 = w.nkv[1];
-      bool ok = warp_all(mbar_wait(BAR(BAR_Q), 0, p.status, kDevTimeoutQ)) &&
-                warp_all(mbar_wait(BAR(BAR_KFULL + 0), 0, p.status, kDevTimeoutKV));
-      if (ok) {
-        tc_fence_after();
-        issue_qk<D, BN, BF16>(tS0, dq0, dk0);
-        umma_commit_w(BAR(BAR_SFULL + 0));
-        if (n1 > 0) {
-          issue_qk<D, BN, BF16>(tS1, dq1, dk0);
-          umma_commit_w(BAR(BAR_SFULL + 1));
-        }
-        umma_commit_w(BAR(BAR_KEMPTY + 0));
-      }
-      for (int j = 0; ok && j < nmax; ++j) {
-        const int vs = j % VST;
-        const int ks1 = (j + 1) % KST;
-        const uint64_t dvj = dv0 + static_cast<uint64_t>((vs * C::kKVBytes) >> 4);
-        const uint64_t dkn = dk0 + static_cast<uint64_t>((ks1 * C::kKVBytes) >> 4);
-        FA_STALL_HERE(j, BAR(BAR_NEVER), p.status, ok)
-        if (!(ok = warp_all(mbar_wait(BAR(BAR_VFULL + vs), (j / VST) & 1, p.status, kDevTimeoutKV)))) break;
-        bool k_ready = false;
-        bool issued_s = false;
-        // tile 0
-        if (j < n0) {
-          if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULLA + 0), j & 1, p.status, kDevTimeoutP)))) break;
+      if constexpr (s_double<BN>()) {
+        // Two S buffers per tile: S(j) in buffer j % 2.  S(0) and S(1) up front, then in step j
+        // P(j) V reads buffer j % 2 and S(j+2) is issued into it right behind.
+        static_assert(KST >= 3, "S two steps ahead needs three K stages");
+        bool ok = warp_all(mbar_wait(BAR(BAR_Q), 0, p.status, kDevTimeoutQ)) &&
+                  warp_all(mbar_wait(BAR(BAR_KFULL + 0), 0, p.status, kDevTimeoutKV));
+        if (ok) {
           tc_fence_after();
-          issue_pv_half<D, BN, BF16>(tO0, tS0, dvj, j > 0 ? 1u : 0u, 0);
-          if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULLB + 0), j & 1, p.status, kDevTimeoutP)))) break;
-          tc_fence_after();
-          issue_pv_half<D, BN, BF16>(tO0, tS0, dvj, 1u, 1);
-          if (j + 1 == n0) {
-            umma_commit_w(BAR(BAR_OFULL + 0));
-          } else {
-            if (!(ok = warp_all(mbar_wait(BAR(BAR_KFULL + ks1), ((j + 1) / KST) & 1, p.status, kDevTimeoutKV)))) break;
-            tc_fence_after();
-            k_ready = true;
-            issue_qk<D, BN, BF16>(tS0, dq0, dkn);
-            umma_commit_w(BAR(BAR_SFULL + 0));
-            issued_s = true;
+          issue_qk<D, BN, BF16>(tS0, dq0, dk0);
+          umma_commit_w(BAR(BAR_SFULL + 0));
+          if (n1 > 0) {
+            issue_qk<D, BN, BF16>(tS1, dq1, dk0);
+            umma_commit_w(BAR(BAR_SFULL + 1));
+          }
+          umma_commit_w(BAR(BAR_KEMPTY + 0));
+          if (nmax > 1) {
+            ok = warp_all(mbar_wait(BAR(BAR_KFULL + 1), 0, p.status, kDevTimeoutKV));
+            if (ok) {
+              tc_fence_after();
+              const uint64_t dk1 = dk0 + static_cast<uint64_t>(C::kKVBytes >> 4);
+              if (n0 > 1) {
+                issue_qk<D, BN, BF16>(tS0 + 64, dq0, dk1);
+                umma_commit_w(BAR(BAR_SFULLB + 0));
+              }
+              if (n1 > 1) {
+                issue_qk<D, BN, BF16>(tS1 + 64, dq1, dk1);
+                umma_commit_w(BAR(BAR_SFULLB + 1));
+              }
+              umma_commit_w(BAR(BAR_KEMPTY + 1));
+            }
           }
         }
-        // tile 1
-        if (j < n1) {
-          if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULLA + 1), j & 1, p.status, kDevTimeoutP)))) break;
+        for (int j = 0; ok && j < nmax; ++j) {
+          const int vs = j % VST;
+          const int ks2 = (j + 2) % KST;
+          const uint32_t boff = (j & 1) * 64;
+          const int sbar = (j & 1) ? BAR_SFULLB : BAR_SFULL;
+          const uint64_t dvj = dv0 + static_cast<uint64_t>((vs * C::kKVBytes) >> 4);
+          const uint64_t dk2 = dk0 + static_cast<uint64_t>((ks2 * C::kKVBytes) >> 4);
+          FA_STALL_HERE(j, BAR(BAR_NEVER), p.status, ok)
+          if (!(ok = warp_all(mbar_wait(BAR(BAR_VFULL + vs), (j / VST) & 1, p.status, kDevTimeoutKV)))) break;
+          bool k_ready = false;
+          bool issued_s = false;
+          // tile 0
+          if (j < n0) {
+            if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULLA + 0), j & 1, p.status, kDevTimeoutP)))) break;
+            tc_fence_after();
+            issue_pv_half<D, BN, BF16>(tO0, tS0 + boff, dvj, j > 0 ? 1u : 0u, 0);
+            if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULLB + 0), j & 1, p.status, kDevTimeoutP)))) break;
+            tc_fence_after();
+            issue_pv_half<D, BN, BF16>(tO0, tS0 + boff, dvj, 1u, 1);
+            umma_commit_w(BAR(BAR_PVDONE + 0));
+            if (j + 1 == n0) {
+              umma_commit_w(BAR(BAR_OFULL + 0));
+            } else if (j + 2 < n0) {
+              if (!(ok = warp_all(mbar_wait(BAR(BAR_KFULL + ks2), ((j + 2) / KST) & 1, p.status, kDevTimeoutKV)))) break;
+              tc_fence_after();
+              k_ready = true;
+              issue_qk<D, BN, BF16>(tS0 + boff, dq0, dk2);
+              umma_commit_w(BAR(sbar + 0));
+              issued_s = true;
+            }
+          }
+          // tile 1
+          if (j < n1) {
+            if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULLA + 1), j & 1, p.status, kDevTimeoutP)))) break;
+            tc_fence_after();
+            issue_pv_half<D, BN, BF16>(tO1, tS1 + boff, dvj, j > 0 ? 1u : 0u, 0);
+            if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULLB + 1), j & 1, p.status, kDevTimeoutP)))) break;
+            tc_fence_after();
+            issue_pv_half<D, BN, BF16>(tO1, tS1 + boff, dvj, 1u, 1);
+            umma_commit_w(BAR(BAR_PVDONE + 1));
+            if (j + 1 == n1) {
+              umma_commit_w(BAR(BAR_OFULL + 1));
+            } else if (j + 2 < n1) {
+              if (!k_ready) {
+                if (!(ok = warp_all(mbar_wait(BAR(BAR_KFULL + ks2), ((j + 2) / KST) & 1, p.status, kDevTimeoutKV)))) break;
+                tc_fence_after();
+              }
+              issue_qk<D, BN, BF16>(tS1 + boff, dq1, dk2);
+              umma_commit_w(BAR(sbar + 1));
+              issued_s = true;
+            }
+          }
+          if (issued_s) umma_commit_w(BAR(BAR_KEMPTY + ks2));  // K(j+2) read by every tile that needs it
+          umma_commit_w(BAR(BAR_VEMPTY + vs));                 // V(j) read by every tile that needs it
+        }
+      } else {
+        bool ok = warp_all(mbar_wait(BAR(BAR_Q), 0, p.status, kDevTimeoutQ)) &&
+                  warp_all(mbar_wait(BAR(BAR_KFULL + 0), 0, p.status, kDevTimeoutKV));
+        if (ok) {
           tc_fence_after();
-          issue_pv_half<D, BN, BF16>(tO1, tS1, dvj, j > 0 ? 1u : 0u, 0);
-          if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULLB + 1), j & 1, p.status, kDevTimeoutP)))) break;
-          tc_fence_after();
-          issue_pv_half<D, BN, BF16>(tO1, tS1, dvj, 1u, 1);
-          if (j + 1 == n1) {
-            umma_commit_w(BAR(BAR_OFULL + 1));
-          } else {
-            if (!k_ready) {
+          issue_qk<D, BN, BF16>(tS0, dq0, dk0);
+          umma_commit_w(BAR(BAR_SFULL + 0));
+          if (n1 > 0) {
+            issue_qk<D, BN, BF16>(tS1, dq1, dk0);
+            umma_commit_w(BAR(BAR_SFULL + 1));
+          }
+          umma_commit_w(BAR(BAR_KEMPTY + 0));
+        }
+        for (int j = 0; ok && j < nmax; ++j) {
+          const int vs = j % VST;
+          const int ks1 = (j + 1) % KST;
+          const uint64_t dvj = dv0 + static_cast<uint64_t>((vs * C::kKVBytes) >> 4);
+          const uint64_t dkn = dk0 + static_cast<uint64_t>((ks1 * C::kKVBytes) >> 4);
+          FA_STALL_HERE(j, BAR(BAR_NEVER), p.status, ok)
+          if (!(ok = warp_all(mbar_wait(BAR(BAR_VFULL + vs), (j / VST) & 1, p.status, kDevTimeoutKV)))) break;
+          bool k_ready = false;
+          bool issued_s = false;
+          // tile 0
+          if (j < n0) {
+            if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULLA + 0), j & 1, p.status, kDevTimeoutP)))) break;
+            tc_fence_after();
+            issue_pv_half<D, BN, BF16>(tO0, tS0, dvj, j > 0 ? 1u : 0u, 0);
+            if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULLB + 0), j & 1, p.status, kDevTimeoutP)))) break;
+            tc_fence_after();
+            issue_pv_half<D, BN, BF16>(tO0, tS0, dvj, 1u, 1);
+            if (j + 1 == n0) {
+              umma_commit_w(BAR(BAR_OFULL + 0));
+            } else {
               if (!(ok = warp_all(mbar_wait(BAR(BAR_KFULL + ks1), ((j + 1) / KST) & 1, p.status, kDevTimeoutKV)))) break;
               tc_fence_after();
+              k_ready = true;
+              issue_qk<D, BN, BF16>(tS0, dq0, dkn);
+              umma_commit_w(BAR(BAR_SFULL + 0));
+              issued_s = true;
             }
-            issue_qk<D, BN, BF16>(tS1, dq1, dkn);
-            umma_commit_w(BAR(BAR_SFULL + 1));
-            issued_s = true;
           }
+          // tile 1
+          if (j < n1) {
+            if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULLA + 1), j & 1, p.status, kDevTimeoutP)))) break;
+            tc_fence_after();
+            issue_pv_half<D, BN, BF16>(tO1, tS1, dvj, j > 0 ? 1u : 0u, 0);
+            if (!(ok = warp_all(mbar_wait(BAR(BAR_PFULLB + 1), j & 1, p.status, kDevTimeoutP)))) break;
+            tc_fence_after();
+            issue_pv_half<D, BN, BF16>(tO1, tS1, dvj, 1u, 1);
+            if (j + 1 == n1) {
+              umma_commit_w(BAR(BAR_OFULL + 1));
+            } else {
+              if (!k_ready) {
+                if (!(ok = warp_all(mbar_wait(BAR(BAR_KFULL + ks1), ((j + 1) / KST) & 1, p.status, kDevTimeoutKV)))) break;
+                tc_fence_after();
+              }
+              issue_qk<D, BN, BF16>(tS1, dq1, dkn);
+              umma_commit_w(BAR(BAR_SFULL + 1));
+              issued_s = true;
+            }
+          }
+          if (issued_s) umma_commit_w(BAR(BAR_KEMPTY + ks1));  // K(j+1) read by every tile that needs it
+          umma_commit_w(BAR(BAR_VEMPTY + vs));                 // V(j) read by every tile that needs it
         }
-        if (issued_s) umma_commit_w(BAR(BAR_KEMPTY + ks1));  // K(j+1) read by every tile that needs it
-        umma_commit_w(BAR(BAR_VEMPTY + vs));                 // V(j) read by every tile that needs it
       }
       // All MMAs issued by this warp must finish before TMEM is released.
       umma_commit_w(BAR(BAR_DRAIN));
@@ -460,11 +562,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       float l = 0.f;
       bool ok = true;
       for (int j = 0; j < nkv; ++j) {
-        if (!(ok = warp_all(mbar_wait<kSoftmaxCopy>(BAR(BAR_SFULL + t), j & 1, p.status, kDevTimeoutS)))) break;
+        // S(j): one buffer per tile, or (64-key tiles) buffer j % 2 of two
+        const bool buf1 = s_double<BN>() && (j & 1);
+        const uint32_t tSj = buf1 ? tS + 64 : tS;
+        const int sbar = (buf1 ? BAR_SFULLB : BAR_SFULL) + t;
+        const uint32_t sphase = s_double<BN>() ? (j >> 1) & 1 : j & 1;
+        if (!(ok = warp_all(mbar_wait<kSoftmaxCopy>(BAR(sbar), sphase, p.status, kDevTimeoutS)))) break;
         tc_fence_after();
         uint32_t r[NCH][32];
 #pragma unroll
-        for (int c = 0; c < NCH; ++c) tmem_ld32(tS + c * 32, r[c]);
+        for (int c = 0; c < NCH; ++c) tmem_ld32(tSj + c * 32, r[c]);
 #pragma unroll
         for (int c = 0; c < NCH; ++c) tmem_ld_wait(r[c]);
         const int kbase = j * BN;
@@ -492,10 +599,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < NCH; ++c) {
             uint32_t pk[16];
             softmax_chunk<BF16, 0>(r[c], scale2, negm2, sum2, pk);
-            tmem_st16(tS + c * 16, pk);
+            tmem_st16(tSj + c * 16, pk);
           }
-          // Rescale the running O if any row's max moved (P V of tile j-1 is complete: it was
-          // issued before S_t(j), whose completion we waited for).
+          // Rescale the running O if any row's max moved.  P V of step j-1 must be complete: with
+          // one S buffer it was issued before S_t(j), whose completion we waited for; with two,
+          // its own barrier says so.
+          if (s_double<BN>() && j > 0)
+            if (!(ok = warp_all(mbar_wait<kSoftmaxCopy>(BAR(BAR_PVDONE + t), (j - 1) & 1, p.status, kDevTimeoutO))))
+              break;
           if (j > 0 && __any_sync(0xffffffffu, upd)) rescale_o<D>(tO, alpha);
           m_used = m_new;
           tmem_st_wait();
@@ -512,10 +623,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < NCH / 2; ++c) {
             uint32_t pk[16];
             softmax_chunk<BF16, poly_pairs<BN>()>(r[c], scale2, negm2, sum2, pk);
-            tmem_st16(tS + c * 16, pk);
+            tmem_st16(tSj + c * 16, pk);
           }
           const float mt = row_max<NCH>(r) * scale;
           const bool upd = mt > m_used + kRescaleThreshold;
+          if (s_double<BN>())  // P V of step j-1 is complete before O may be rescaled
+            if (!(ok = warp_all(mbar_wait<kSoftmaxCopy>(BAR(BAR_PVDONE + t), (j - 1) & 1, p.status, kDevTimeoutO))))
+              break;
           if (__any_sync(0xffffffffu, upd)) {
             const float m_new = upd ? mt : m_used;
             alpha = ex2_approx(m_used - m_new);
@@ -526,7 +640,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = 0; c < NCH / 2; ++c) {
               uint32_t pk[16];
               softmax_chunk<BF16, 0>(r[c], scale2, negm2, sum2, pk);
-              tmem_st16(tS + c * 16, pk);
+              tmem_st16(tSj + c * 16, pk);
             }
             rescale_o<D>(tO, alpha);
             m_used = m_new;
@@ -538,7 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = NCH / 2; c < NCH; ++c) {
             uint32_t pk[16];
             softmax_chunk<BF16, poly_pairs<BN>()>(r[c], scale2, negm2, sum2, pk);
-            tmem_st16(tS + c * 16, pk);
+            tmem_st16(tSj + c * 16, pk);
           }
           tmem_st_wait();
           tc_fence_before();
