@@ -513,7 +513,7 @@ struct DkdvCfg {
   static constexpr int kTile = kBT * D * 2;
   static constexpr int kStat = kBT * 4;  // one LSE (or delta) slice of a query tile
   static constexpr int kBudget = kSmemOptin - 256;
-  static constexpr int kDOStages = 2;    // dO is released early (after dV), two stages suffice
+  static constexpr int kDOStages = 2;    // dO is released after dS^T (before dK's Q), two stages suffice
   static constexpr int kQFit = (kBudget - 2 * kTile - kDOStages * (kTile + kStat)) / (kTile + kStat);
   static constexpr int kQStages = kQFit > 4 ? 4 : kQFit;  // Q is held until dK, so it gets more
   static_assert(kQStages >= 3, "need a triple-buffered Q ring");
@@ -658,7 +658,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (!(ok = warp_all(mbar_wait(BAR(KV_PREADY), s & 1, p.status, kDevTimeoutBwd)))) break;
           tc_fence_after();
           umma_tmem_tile<D, BF16>(tDV, tST, desc_add(dOm, os * C::kTile), s > 0 ? 1u : 0u);  // dV += P^T dO
-          umma_commit_w(BAR(KV_OEMPTY + os));  // dO(s): read by dP^T(s) and dV(s)
           if (s + 1 < nsteps) {
             const int q1 = (s + 1) % QST;
             if (!(ok = warp_all(mbar_wait(BAR(KV_QFULL + q1), ((s + 1) / QST) & 1, p.status, kDevTimeoutBwd)))) break;
@@ -670,6 +669,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           tc_fence_after();
           umma_tmem_tile<D, BF16>(tDK, tDPT, desc_add(dQm, qs * C::kTile), s > 0 ? 1u : 0u);  // dK += dS^T Q
           umma_commit_w(BAR(KV_QEMPTY + qs));  // Q(s): read by S^T(s) and dK(s)
+          // dO(s) stage: its tile is read by dP^T(s) and dV(s), its delta slice by the compute
+          // warpgroups while they form dS^T(s), which DSREADY(s) has just confirmed is done.
+          umma_commit_w(BAR(KV_OEMPTY + os));
           if (s + 1 < nsteps) {
             const int o1 = (s + 1) % OST;
             if (!(ok = warp_all(mbar_wait(BAR(KV_OFULL + o1), ((s + 1) / OST) & 1, p.status, kDevTimeoutBwd)))) break;
