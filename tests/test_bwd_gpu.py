@@ -141,8 +141,8 @@ def test_backward_deterministic(cuda_device):
 
 @pytest.mark.parametrize("H_kv,dtype", [(32, torch.float16), (8, torch.bfloat16)])
 def test_backward_kernels_repeat_bit_for_bit_at_full_size(H_kv, dtype, cuda_device):
-    """dK/dV and dQ run 40 times on one full-size input (B=4 H=32 S=8192 D=128) give the same bits
-    every time.  The dK/dV kernel reads each query tile's delta slice from the shared-memory stage
+    """dK/dV, dQ and the forward (64- and 128-key tiles) run 40 times on one full-size input
+    (B=4 H=32 S=8192 D=128) give the same bits every time.  The dK/dV kernel reads each query tile's delta slice from the shared-memory stage
     of its dO tile; a stage released as soon as dV had read the tile (before the compute warps had
     read the slice) let the next dO load overwrite the slice in rare runs (dK off by a few fp16
     ulps in 17 of 150 runs of this MHA input)."""
@@ -158,12 +158,15 @@ def test_backward_kernels_repeat_bit_for_bit_at_full_size(H_kv, dtype, cuda_devi
     first = None
     for _ in range(40):
         dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        o64, o128 = torch.empty_like(q), torch.empty_like(q)
         nat.bwd_dkdv(q, k, v, do, lse, delta, dk, dv, 64, 128)
         nat.bwd_dq(q, k, v, do, lse, delta, dq, 64, 128)
+        nat.fwd(q, k, v, o64, None, 64, 64)    # the forward with both K/V tiles, too
+        nat.fwd(q, k, v, o128, None, 64, 128)
         if first is None:
-            first = (dq, dk, dv)
+            first = (dq, dk, dv, o64, o128)
             continue
-        for name, x, y in zip(("dQ", "dK", "dV"), (dq, dk, dv), first):
+        for name, x, y in zip(("dQ", "dK", "dV", "O 64-key", "O 128-key"), (dq, dk, dv, o64, o128), first):
             assert torch.equal(x, y), name
     nat.check_status(cuda_device)
 
