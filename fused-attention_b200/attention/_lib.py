@@ -24,7 +24,7 @@ ABI_VERSION = 1
 def kv_tile(tile_n):
     """K/V tile (keys per tile) of the forward kernel for the reference's `tile_n` knob: the sm_100a
     forward has 64- and 128-key variants, so tile_n <= 64 runs the 64-key tile and larger tile_n
-    the 128-key tile (the faster one on B200: 15-18 % at N = 8192).  The query side always runs
+    the 128-key tile (the faster one on B200: 18-19 % at N = 8192).  The query side always runs
     128-row tcgen05 tiles, so tile_m takes part only in the caller's divisibility rule."""
     return 64 if int(tile_n) <= 64 else 128
 
