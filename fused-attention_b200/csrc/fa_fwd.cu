@@ -31,7 +31,8 @@
 // a softmax warp waiting forever).  The teardown after the role branches runs under both budgets.
 // TMEM (512 columns): S_0 | S_1 | O_0 | O_1, 128 columns each; P_t (16-bit) overwrites the first
 // BN/2 columns of S_t once the row is in registers.  With 64-key tiles S_t takes 64 of the tile's
-// 128 columns, so each tile has two S buffers and Q K^T runs two steps ahead of P V.  The two tiles ping-pong: while one tile's
+// 128 columns, so each tile has two S buffers and Q K^T runs two steps ahead of P V (O is then
+// rescaled only after a per-tile "P V done" barrier).  The two tiles ping-pong: while one tile's
 // warpgroup turns S into P, the tensor core runs the other tile's P V and next Q K^T.  P is
 // published in two halves (keys [0, BN/2) and [BN/2, BN)), so the first half's P V runs while the
 // second half is exponentiated; on interior tiles the first half uses the running max, and the
