@@ -211,6 +211,23 @@ def run_reference_arm(a, rank):
     print(json.dumps(line), flush=True)
 
 
+def e2e_slices(B, H, H_kv, world, max_slices):
+    """The end-to-end leg's pipeline slices: [(q/o/dq/do index, k/v/dk/dv index)], each a pair of
+    (batch slice, head slice).  A slice is `world` batch entries; on one GPU each batch entry is
+    also cut into 2^k runs of whole K/V-head groups (query heads [g*grp, (g+1)*grp) go with K/V
+    head g), as many as keep the step at or under `max_slices` slices."""
+    bs = world
+    hsplit = 1
+    if world == 1:
+        while hsplit * 2 * (B // bs) <= max_slices and H_kv % (hsplit * 2) == 0:
+            hsplit *= 2
+    kvh = H_kv // hsplit
+    qh = kvh * (H // H_kv)
+    return [((slice(c * bs, (c + 1) * bs), slice(p * qh, (p + 1) * qh)),
+             (slice(c * bs, (c + 1) * bs), slice(p * kvh, (p + 1) * kvh)))
+            for c in range(B // bs) for p in range(hsplit)]
+
+
 def workload_config(a, world):
     kind = "GQA" if a.kv_heads and a.kv_heads != a.heads else "MHA"
     if a.strong:
@@ -387,16 +404,7 @@ def main():
     h2d_stream = torch.cuda.Stream(device=dev)
     d2h_stream = torch.cuda.Stream(device=dev)
     comp = torch.cuda.current_stream(dev)
-    bs = world
-    hsplit = 1
-    if world == 1:
-        while hsplit * 2 * (B // bs) <= a.e2e_slices and H_kv % (hsplit * 2) == 0:
-            hsplit *= 2
-    kvh = H_kv // hsplit
-    qh = kvh * (H // H_kv)
-    slices = [((slice(c * bs, (c + 1) * bs), slice(p * qh, (p + 1) * qh)),
-               (slice(c * bs, (c + 1) * bs), slice(p * kvh, (p + 1) * kvh)))
-              for c in range(B // bs) for p in range(hsplit)]
+    slices = e2e_slices(B, H, H_kv, world, a.e2e_slices)
     nslices = len(slices)
 
     def e2e_step():

@@ -72,3 +72,31 @@ def test_csv_kernel_columns_name_no_machine_path():
     assert fb.kernel_label(fb.DEFAULT_KERNEL) == "fused-attention_b200/attention/fused/fused.py"
     assert fb.kernel_label("/elsewhere/custom_kernel.py") == "custom_kernel.py"
     assert [fb.kernel_tiles(n) for n in (32, 64, 128, 256)] == ["q128_kv64", "q128_kv64", "q128_kv128", "q128_kv128"]
+
+
+def _bench():
+    spec = importlib.util.spec_from_file_location("_t_bench", os.path.join(REPO, "bench.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+@pytest.mark.parametrize("B,H,H_kv,world,cap,expect", [(4, 32, 32, 1, 32, 32), (8, 32, 8, 1, 32, 32),
+                                                       (4, 32, 32, 1, 16, 16), (8, 32, 8, 1, 64, 64),
+                                                       (32, 32, 32, 8, 32, 4), (8, 32, 8, 8, 32, 1)])
+def test_e2e_slices_cover_every_head_once_in_whole_groups(B, H, H_kv, world, cap, expect):
+    """bench.py's end-to-end slices: every (batch, query head) and (batch, K/V head) lands in
+    exactly one slice, each slice pairs K/V head g with query heads [g*grp, (g+1)*grp), and the
+    count respects the cap (one GPU) or is one slice per `world` batch entries (several GPUs)."""
+    slices = _bench().e2e_slices(B, H, H_kv, world, cap)
+    assert len(slices) == expect
+    grp = H // H_kv
+    seen_q, seen_kv = set(), set()
+    for (bq, hq), (bk, hk) in slices:
+        assert bq == bk and bq.stop - bq.start == world
+        assert hq.start == hk.start * grp and hq.stop == hk.stop * grp
+        seen_q |= {(b, h) for b in range(bq.start, bq.stop) for h in range(hq.start, hq.stop)}
+        seen_kv |= {(b, h) for b in range(bk.start, bk.stop) for h in range(hk.start, hk.stop)}
+    assert seen_q == {(b, h) for b in range(B) for h in range(H)}
+    assert seen_kv == {(b, h) for b in range(B) for h in range(H_kv)}
+    assert sum((q[0].stop - q[0].start) * (q[1].stop - q[1].start) for q, _ in slices) == B * H
