@@ -606,8 +606,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           // one S buffer it was issued before S_t(j), whose completion we waited for; with two,
           // its own barrier says so.
           if (s_double<BN>() && j > 0)
-            if (!(ok = warp_all(mbar_wait<kSoftmaxCopy>(BAR(BAR_PVDONE + t), (j - 1) & 1, p.status, kDevTimeoutO))))
+            if (!(ok = warp_all(mbar_wait<kSoftmaxCopy>(BAR(BAR_PVDONE + t), (j - 1) & 1, p.status, kDevTimeoutO)))) {
+              tmem_st_wait();  // no TMEM store of this thread left in flight at teardown
               break;
+            }
           if (j > 0 && __any_sync(0xffffffffu, upd)) rescale_o<D>(tO, alpha);
           m_used = m_new;
           tmem_st_wait();
@@ -629,8 +631,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float mt = row_max<NCH>(r) * scale;
           const bool upd = mt > m_used + kRescaleThreshold;
           if (s_double<BN>())  // P V of step j-1 is complete before O may be rescaled
-            if (!(ok = warp_all(mbar_wait<kSoftmaxCopy>(BAR(BAR_PVDONE + t), (j - 1) & 1, p.status, kDevTimeoutO))))
+            if (!(ok = warp_all(mbar_wait<kSoftmaxCopy>(BAR(BAR_PVDONE + t), (j - 1) & 1, p.status, kDevTimeoutO)))) {
+              tmem_st_wait();  // no TMEM store of this thread left in flight at teardown
               break;
+            }
           if (__any_sync(0xffffffffu, upd)) {
             const float m_new = upd ? mt : m_used;
             alpha = ex2_approx(m_used - m_new);

@@ -94,7 +94,7 @@ def _stall_lib():
     return lib
 
 
-@pytest.mark.parametrize("kernel", ["forward", "dkdv", "dq"])
+@pytest.mark.parametrize("kernel", ["forward", "forward64", "dkdv", "dq"])
 def test_pipeline_wait_runs_out_and_the_device_stays_usable(kernel, cuda_device):
     nat = _nat()
     lib = _stall_lib()
@@ -108,8 +108,9 @@ def test_pipeline_wait_runs_out_and_the_device_stays_usable(kernel, cuda_device)
     stream = P(torch.cuda.current_stream(cuda_device).cuda_stream)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    if kernel == "forward":
-        rc = lib.fa_fwd(ptr(q), ptr(k), ptr(v), ptr(out), ptr(lse), B, H, H, S, D, 0, 64, 128, ptr(status), stream)
+    if kernel in ("forward", "forward64"):  # 128-key tiles, and 64-key tiles (two S buffers per tile)
+        tile_n = 128 if kernel == "forward" else 64
+        rc = lib.fa_fwd(ptr(q), ptr(k), ptr(v), ptr(out), ptr(lse), B, H, H, S, D, 0, 64, tile_n, ptr(status), stream)
     elif kernel == "dkdv":
         rc = lib.fa_bwd_dkdv(ptr(q), ptr(k), ptr(v), ptr(do), ptr(lse), ptr(delta), ptr(out_k), ptr(out_v),
                              B, H, H, S, D, 0, 64, 128, ptr(status), stream)
